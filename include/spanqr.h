@@ -1,0 +1,130 @@
+/*
+ * spanqr_b200 -- C ABI of the B200-native orth(X) (libspanqr.so).
+ *
+ * orth(X): an orthonormal basis Q of the column span of a tall fp32 matrix X [K, r] (K >= r), by the robust
+ * shifted Cholesky-QR recipe of oguzeldereli/spanqr (power-of-2 scale, seeded dust, three shifted and clamped
+ * Cholesky-QR passes with blocked triangular solves, two Newton-Schulz polish steps).
+ *
+ * Conventions for every entry point:
+ *   - all matrix pointers are DEVICE pointers on the current CUDA device, row-major fp32, 16-byte aligned, with
+ *     leading dimensions (in elements) that are multiples of 4;
+ *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream) and never synchronises the host;
+ *   - the caller owns every buffer, including the workspace `ws` (size from spanqr_workspace_bytes, 256-byte
+ *     aligned); the library allocates no device memory on these paths;
+ *   - calls in flight at the same time (on different streams or threads) need different workspaces;
+ *   - the return value is SPANQR_OK or an error code (spanqr_strerror); nothing is enqueued on an error.
+ *
+ * Reference interfaces these replace (file:line in oguzeldereli/spanqr):
+ *   spanqr_orth_f32          orth.py:13-20 -> candidates/kcholqr.py:112-132 kcholqr_f(X)
+ *   spanqr_orth_strided_f32  no reference counterpart: a batch of same-shape layers (orth_batched)
+ *   spanqr_orth_batched_f32  no reference counterpart: same, from device arrays of matrix pointers
+ *   spanqr_orth_ptrs_f32     no reference counterpart: same, from host arrays of matrix pointers
+ *   spanqr_gram_f32          candidates/tri.py:362-375 gram_f(Y, s) and tri.py:285-297 gram_split(Y, bt=64)
+ *   spanqr_chol_f32          candidates/kchol.py:35-44 chol32(G, tau) (kernel candidates/cuk/chol.cu:273-276)
+ *   spanqr_trsm_f32          candidates/tri.py:406-412 trsm_f(X, L, Li, s, Z, eps)
+ */
+#ifndef SPANQR_H
+#define SPANQR_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* spanqr_stream_t; /* the same type as cudaStream_t */
+
+enum spanqr_status {
+    SPANQR_OK = 0,
+    SPANQR_ERR_SHAPE = 1,     /* r not a multiple of 32, r > 512, K < r, batch < 1 (no Householder fallback)   */
+    SPANQR_ERR_ARG = 2,       /* null or misaligned pointer, leading dimension too small or not a multiple of 4 */
+    SPANQR_ERR_WORKSPACE = 3, /* workspace too small or not 256-byte aligned                                    */
+    SPANQR_ERR_CUDA = 4,      /* a CUDA runtime call or kernel launch failed                                    */
+    SPANQR_ERR_DEVICE = 5     /* the device status word reports a failure (spanqr_read_status)                  */
+};
+
+/* version as MAJOR * 10000 + MINOR * 100 + PATCH */
+int spanqr_version(void);
+
+/* human-readable text for a status code */
+const char* spanqr_strerror(int code);
+
+/* text of the last CUDA error seen by this library on the calling thread ("" if none) */
+const char* spanqr_last_cuda_error(void);
+
+/* Bytes of workspace a call with `batch` matrices of shape K x r needs (the same for orth, strided and batched). */
+int spanqr_workspace_bytes(int K, int r, int batch, size_t* bytes);
+
+/*
+ * Q = orth(X).  X [K, r] (leading dimension ldx) is read only; Q [K, r] (ldq) is written.  Z [K, r] (leading
+ * dimension r) is the dust: the reference draws it once per shape with torch.randn on the CUDA generator seeded
+ * 20261018 and divides each column by its norm (kcholqr.py:103-109); the caller passes it in.
+ */
+int spanqr_orth_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z,
+                    void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/* orth of `batch` same-shape matrices X + b*strideX -> Q + b*strideQ, all sharing the dust Z.
+ * Each matrix gets exactly the bits spanqr_orth_f32 would give it, whatever the batch. */
+int spanqr_orth_strided_f32(const float* X, long long ldx, long long strideX, float* Q, long long ldq,
+                            long long strideQ, int K, int r, int batch, const float* Z, void* ws, size_t ws_bytes,
+                            spanqr_stream_t stream);
+
+/* the same with DEVICE arrays of per-matrix pointers dX[batch], dQ[batch] (leading dimension r for all; every
+ * pointer 16-byte aligned) */
+int spanqr_orth_batched_f32(const float* const* dX, float* const* dQ, int K, int r, int batch, const float* Z,
+                            void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/* the same with HOST arrays hX[batch], hQ[batch] of device pointers (copied into kernel parameters, so no
+ * host-to-device copy and no pinned memory is involved; leading dimension r for all) */
+int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r, int batch, const float* Z,
+                         void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * Component entry points (the reference's kernel modules), for tests and for callers that compose their own
+ * recipe.  Each needs its own workspace of spanqr_workspace_bytes(K or n, n, 1) bytes.
+ *
+ * spanqr_gram_f32: G [n, n] = A^T A for A = s * Y (Y [K, n], leading dimension ldy), split-K with a compensated
+ *   (Kahan) sum inside each split and an fp64 sum across splits; d_s: device pointer to the fp32 scale s, or NULL
+ *   for s = 1.  G is written in full (both triangles, exactly symmetric).
+ */
+int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_s, float* G, void* ws,
+                    size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * spanqr_chol_f32: lower Cholesky factor of G [n, n] (lower triangle read, G left unchanged) with every pivot
+ *   clamped from below at *d_tau (a NaN pivot also becomes tau): L [n, n] (zeros above the diagonal) and
+ *   Li [n, 32], the inverses of L's 32 x 32 diagonal tiles stacked.  n a multiple of 32, at most 512.
+ */
+int spanqr_chol_f32(const float* G, int n, const float* d_tau, float* L, float* Li, void* ws, size_t ws_bytes,
+                    spanqr_stream_t stream);
+
+/*
+ * spanqr_trsm_f32: Y = (s X + eps Z) L^-T with L, Li from spanqr_chol_f32; X [K, n] (ldx), Y [K, n] (ldy),
+ *   Z [K, n] (leading dimension n) or NULL, d_s device pointer to s or NULL for s = 1.  Y may equal X (in place).
+ */
+int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* d_s, float eps, const float* L,
+                    const float* Li, int K, int n, float* Y, long long ldy, spanqr_stream_t stream);
+
+/*
+ * Kernel timing (no reference counterpart; the reference stamps %globaltimer under CHOL_DEBUG, chol.cu:17-23).
+ * While enabled, the orth entry points bracket every kernel they launch with CUDA events on the launching stream.
+ * spanqr_timing_collect waits for those events, adds each kernel's duration to ms[kind] and one to launches[kind]
+ * for kind < nkinds, and forgets them.  Kinds are numbered 0..spanqr_kernel_kinds()-1 (names from
+ * spanqr_kernel_kind_name).  Timing state is per host thread.
+ */
+int spanqr_timing_enable(int on);
+int spanqr_timing_collect(double* ms, long long* launches, int nkinds);
+int spanqr_kernel_kinds(void);
+const char* spanqr_kernel_kind_name(int kind);
+
+/*
+ * Reads the device status word of a workspace (0 = no failure recorded by the last call that used it).
+ * This call synchronises `stream`.
+ */
+int spanqr_read_status(const void* ws, spanqr_stream_t stream, int* device_status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPANQR_H */

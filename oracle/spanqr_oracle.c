@@ -321,16 +321,25 @@ void oracle_trsm(const float* X, long long ldx, const float* Z, float s, int has
     }
 }
 
-/* Frobenius norm (torch.linalg.matrix_norm, kcholqr.py:127): squares summed in fp64, rounded to fp32 */
+/* Frobenius norm (torch.linalg.matrix_norm, kcholqr.py:127): squares summed in fp64, one row at a time (columns
+ * in order), then the row sums in order; rounded to fp32 after the square root. */
 float oracle_fro(const float* G, int n) {
-    double acc = 0.0;
-    for (size_t i = 0; i < (size_t)n * n; ++i) acc += (double)G[i] * (double)G[i];
-    return (float)sqrt(acc);
+    double tot = 0.0;
+    for (int a = 0; a < n; ++a) {
+        double row = 0.0;
+        for (int b = 0; b < n; ++b) {
+            const double g = (double)G[(size_t)a * n + b];
+            row += g * g;
+        }
+        tot += row;
+    }
+    return (float)sqrt(tot);
 }
 
 /* ---------------------------------------------------------------------------------------------------
  * kcholqr.py:36-43 _ns_mm: Newton-Schulz as a correction, Y <- Y + Y D with D = 0.5 (I - Y^T Y).
- * Step i < n-1 uses the plain fp32 Gram, the last step the Kahan split Gram (gram_split, bt=64).
+ * The reference takes step i < n-1's Gram from cuBLAS SGEMM (order unspecified) and the last step's from the
+ * Kahan split Gram (gram_split, bt=64); here every step uses the split Gram (at least as accurate, fixed order).
  * D = eye.sub_(G).mul_(0.5) rounds twice; addmm(Y, Y, D) adds the fp32 product to Y.
  * ------------------------------------------------------------------------------------------------- */
 void oracle_ns(float* Y, int K, int n, int steps, int nsm) {
@@ -338,8 +347,7 @@ void oracle_ns(float* Y, int K, int n, int steps, int nsm) {
     float* D = (float*)malloc(sizeof(float) * (size_t)n * n);
     float* Dt = (float*)malloc(sizeof(float) * (size_t)n * n);
     for (int it = 0; it < steps; ++it) {
-        if (it == steps - 1) oracle_gram_kahan(Y, K, n, n, 1.0f, 0, nsm, G);
-        else oracle_gram_plain(Y, K, n, n, G);
+        oracle_gram_kahan(Y, K, n, n, 1.0f, 0, nsm, G);
         for (int a = 0; a < n; ++a)
             for (int b = 0; b < n; ++b) {
                 const float e = (a == b) ? 1.0f : 0.0f;
@@ -368,7 +376,7 @@ void oracle_ns(float* Y, int K, int n, int steps, int nsm) {
 /* ---------------------------------------------------------------------------------------------------
  * kcholqr.py:112-132 kcholqr_f(X, eps=5e-7, alpha=1e-7, tau=1e-8, ns=2):
  *   s = pow2_scale(max|X|); 3 passes of {G = gram (pass 0: Kahan split Gram of s X, dust excluded;
- *   later: plain fp32), nrm = ||G||_F, G_ii += alpha nrm, (L, Li) = chol32(G, tau nrm + 1e-30),
+ *   later: the reference's cuBLAS SGEMM, here the same split Gram), nrm = ||G||_F, G_ii += alpha nrm, (L, Li) = chol32(G, tau nrm + 1e-30),
  *   Y = trsm(Y, L, Li) with s X + eps Z on pass 0}; then _ns_mm(Y, ns).
  * Z: the dust, K x r, unit columns (kcholqr.py:103-109; the caller builds it).
  * Returns 0, or 1 for an unsupported shape (r % 32 != 0; the reference then falls back to Householder).
@@ -384,7 +392,7 @@ int oracle_kcholqr_f(const float* X, long long ldx, const float* Z, int K, int r
     float* Y = (float*)malloc(sizeof(float) * (size_t)K * r);
     for (int p = 0; p < 3; ++p) {
         if (p == 0) oracle_gram_kahan(X, K, r, ldx, s, 1, nsm, G);
-        else oracle_gram_plain(Y, K, r, r, G);
+        else oracle_gram_kahan(Y, K, r, r, 1.0f, 0, nsm, G);
         const float nrm = oracle_fro(G, r);
         const float shift = alpha * nrm;
         for (int i = 0; i < r; ++i) G[(size_t)i * r + i] = G[(size_t)i * r + i] + shift;

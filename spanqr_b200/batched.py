@@ -1,0 +1,142 @@
+"""orth_batched: orth of many independent layer matrices at once, on one GPU or spread over the GPUs of one node.
+
+The reference has no batched entry point (batching same-shape layers is named as future work in METHODS.md:90-93,
+102-103).  Semantics per matrix equal orth(X): every matrix gets exactly the bits orth would give it, whatever the
+batch, the grouping or the number of GPUs (the kernels' arithmetic does not depend on the batch).
+
+Multi-GPU (torch.distributed initialised, one process per GPU): every rank passes the same list of matrices; the
+matrices are partitioned by cost K * r with a deterministic greedy (largest first, to the least-loaded rank, ties to
+the lower rank); each rank computes its share into its slab of one output buffer laid out owner by owner; then the
+slabs are exchanged over NCCL (all_gather_into_tensor when the slabs are equal, else one broadcast per owner), so every
+rank returns every Q.  With gather=False each rank returns only its own Qs (None elsewhere).
+"""
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .core import check_input, aligned, zdust, workspace
+
+
+def partition(costs, world):
+    """owner rank of each matrix.  Equal costs: contiguous blocks (sizes differ by at most one), so the owner-major
+    output order is the index order.  Otherwise: largest cost first, to the least-loaded rank (lowest rank on ties)."""
+    B = len(costs)
+    if B and all(c == costs[0] for c in costs):
+        base, extra = divmod(B, world)
+        owner, q, left = [], 0, base + (1 if extra > 0 else 0)
+        for i in range(B):
+            while left == 0:
+                q += 1
+                left = base + (1 if q < extra else 0)
+            owner.append(q)
+            left -= 1
+        return owner
+    owner = [0] * B
+    loads = [0] * world
+    for i in sorted(range(B), key=lambda i: (-costs[i], i)):
+        w = min(range(world), key=lambda q: (loads[q], q))
+        owner[i] = w
+        loads[w] += costs[i]
+    return owner
+
+
+def layout(numels, owner, world):
+    """offsets of each matrix in the flat output (owner by owner, index order inside a slab), the slab bounds
+    slab[q]..slab[q+1] of each owner and the slab sizes"""
+    order = sorted(range(len(numels)), key=lambda i: (owner[i], i))
+    offs = [0] * len(numels)
+    slab = [0] * (world + 1)
+    off = 0
+    for i in order:
+        offs[i] = off
+        off += numels[i]
+        slab[owner[i] + 1] = off
+    for q in range(1, world + 1):
+        slab[q] = max(slab[q], slab[q - 1])
+    return offs, slab, [slab[q + 1] - slab[q] for q in range(world)]
+
+
+def exchange(out, slab, sizes, group=None):
+    """every rank's slab of `out` to every rank: one all-gather when the slabs are equal, else a broadcast per owner"""
+    rank = dist.get_rank(group)
+    world = len(sizes)
+    if all(sz == sizes[0] for sz in sizes):
+        dist.all_gather_into_tensor(out, out[slab[rank]:slab[rank + 1]], group=group)
+        return
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(world))
+    works = [dist.broadcast(out[slab[q]:slab[q + 1]], src=ranks[q], group=group, async_op=True)
+             for q in range(world) if sizes[q] > 0]
+    for w in works:
+        w.wait()
+
+
+def _run_group(Xs, Qs, stream):
+    """orth of same-shape matrices Xs -> Qs (lists of contiguous aligned tensors) in one library call"""
+    K, r = Xs[0].shape
+    dev = Xs[0].device
+    B = len(Xs)
+    Z = zdust(K, r, dev)
+    ws = workspace(dev, K, r, B, stream)
+    L = _lib.lib()
+    PP = _lib.ctypes.c_void_p * B
+    hx = PP(*[x.data_ptr() for x in Xs])
+    hq = PP(*[q.data_ptr() for q in Qs])
+    _lib.check(L.spanqr_orth_ptrs_f32(_lib.ctypes.cast(hx, _lib.ctypes.c_void_p), _lib.ctypes.cast(hq, _lib.ctypes.c_void_p),
+                                      K, r, B, Z.data_ptr(), ws.data_ptr(), ws.numel(), stream.cuda_stream),
+               f"orth_batched({B}x{K}x{r})")
+
+
+def _run_local(Xs, Qs):
+    """orth of a list of matrices on this GPU, one library call per shape"""
+    if not Xs:
+        return
+    dev = Xs[0].device
+    stream = torch.cuda.current_stream(dev)
+    groups = {}
+    for x, q in zip(Xs, Qs):
+        groups.setdefault(tuple(x.shape), ([], []))
+        groups[tuple(x.shape)][0].append(x)
+        groups[tuple(x.shape)][1].append(q)
+    for xs, qs in groups.values():
+        _run_group(xs, qs, stream)
+
+
+def orth_batched(Xs, *, gather=True, group=None):
+    """Q_i = orth(X_i) for every matrix.  Xs: a list of fp32 CUDA [K_i, r_i] tensors on one device, or one
+    [B, K, r] tensor.  Returns a list of Qs (a [B, K, r] tensor for a tensor input).  Under torch.distributed the
+    work is split across the ranks of `group` (default: the world) and the results all-gathered (gather=True)."""
+    stacked = torch.is_tensor(Xs)
+    if stacked:
+        if Xs.dim() != 3:
+            raise ValueError("a tensor input must be [B, K, r]")
+        Xs = list(Xs.unbind(0))
+    Xs = list(Xs)
+    if stacked and not gather:
+        raise ValueError("gather=False needs a list input")
+    if not Xs:
+        return [] if not stacked else torch.empty(0)
+    for i, x in enumerate(Xs):
+        check_input(x, f"Xs[{i}]")
+    dev = Xs[0].device
+    if any(x.device != dev for x in Xs):
+        raise ValueError("all matrices must be on one device")
+    Xs = [aligned(x) for x in Xs]
+    distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+    world = dist.get_world_size(group) if distributed else 1
+    rank = dist.get_rank(group) if distributed else 0
+    owner = partition([x.shape[0] * x.shape[1] for x in Xs], world)
+
+    offs, slab, sizes = layout([x.numel() for x in Xs], owner, world)
+    with torch.cuda.device(dev):
+        out = torch.empty(slab[world], dtype=torch.float32, device=dev)
+        Qs = [out[offs[i]:offs[i] + Xs[i].numel()].view(Xs[i].shape) for i in range(len(Xs))]
+        mine = [i for i in range(len(Xs)) if owner[i] == rank]
+        _run_local([Xs[i] for i in mine], [Qs[i] for i in mine])
+        if distributed and gather:
+            exchange(out, slab, sizes, group)
+    if distributed and not gather:
+        return [Qs[i] if owner[i] == rank else None for i in range(len(Xs))]
+    if stacked:
+        # equal shapes give a contiguous partition, so the buffer is already in index order
+        return out.view(len(Xs), *Xs[0].shape)
+    return Qs

@@ -1,0 +1,87 @@
+"""orth(X): the drop-in for spanqr's `orth` (orth.py:13-20 -> candidates/kcholqr.py:112-132, kcholqr_f).
+
+    from spanqr_b200 import orth
+    Q = orth(X)      # X: fp32 CUDA [K, r] -> Q: fp32 CUDA [K, r], Q^T Q = I, span(Q) = span(X)
+
+Every call runs on libspanqr's CUDA kernels on the current stream, with no host synchronisation.  There is no
+fallback: an unsupported shape raises (the reference silently falls back to torch.linalg.qr for r % 32 != 0,
+kcholqr.py:118-119, and routes r > 512 to block Gram-Schmidt, orth.py:18-19).
+"""
+import threading
+
+import torch
+
+from . import _lib
+
+TB = 32               # tile width (candidates/kchol.py:9)
+MAX_R = 512
+DUST_SEED = 20261018  # candidates/kcholqr.py:106
+
+_Z = {}
+_WS = {}
+_lock = threading.Lock()
+
+
+def zdust(K, r, device):
+    """The dust Z of kcholqr.py:103-109: torch.randn(K, r) on the device's generator seeded 20261018, each column
+    divided by its norm; cached per (K, r, device).  Drawn with torch on the same device as the reference draws it,
+    so both see the same Z."""
+    device = torch.device(device)
+    key = (K, r, str(device))
+    Z = _Z.get(key)
+    if Z is None:
+        g = torch.Generator(device=device).manual_seed(DUST_SEED)
+        Z = torch.randn(K, r, device=device, generator=g)
+        Z = Z / Z.norm(dim=0, keepdim=True)
+        with _lock:
+            Z = _Z.setdefault(key, Z)
+    return Z
+
+
+def workspace(device, K, r, batch=1, stream=None):
+    """a cached device workspace for (device, stream, K, r, batch); calls on different streams never share one"""
+    device = torch.device(device)
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
+    key = (str(device), stream.cuda_stream, K, r, batch)
+    ws = _WS.get(key)
+    if ws is None:
+        ws = torch.empty(_lib.workspace_bytes(K, r, batch), dtype=torch.uint8, device=device)
+        with _lock:
+            ws = _WS.setdefault(key, ws)
+    return ws
+
+
+def check_input(X, name="X"):
+    if not torch.is_tensor(X) or X.dim() != 2:
+        raise ValueError(f"{name} must be a 2-D tensor [K, r]")
+    if X.dtype != torch.float32 or not X.is_cuda:
+        raise TypeError(f"{name} must be an fp32 CUDA tensor (got {X.dtype} on {X.device})")
+    K, r = X.shape
+    if r % TB or r < TB or r > MAX_R or K < r:
+        raise ValueError(f"unsupported shape {K}x{r}: r must be a multiple of {TB} in [{TB}, {MAX_R}] and K >= r")
+
+
+def aligned(X):
+    """X itself when contiguous and 16-byte aligned, else a fresh contiguous copy (torch allocations are aligned)"""
+    if X.is_contiguous() and X.data_ptr() % 16 == 0:
+        return X
+    return X.clone(memory_format=torch.contiguous_format)
+
+
+def orth(X: torch.Tensor) -> torch.Tensor:
+    """Orthonormal basis of the column span of X (fp32 CUDA, K >= r, r a multiple of 32 up to 512).  Where X is
+    rank-deficient or zero, the missing directions are completed with arbitrary orthonormal ones (never zero or NaN
+    columns).  Deterministic, no host sync, X left untouched."""
+    check_input(X)
+    X = aligned(X)
+    K, r = X.shape
+    dev = X.device
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        Z = zdust(K, r, dev)
+        Q = torch.empty((K, r), dtype=torch.float32, device=dev)
+        ws = workspace(dev, K, r, 1, stream)
+        _lib.check(_lib.lib().spanqr_orth_f32(X.data_ptr(), r, Q.data_ptr(), r, K, r, Z.data_ptr(), ws.data_ptr(),
+                                              ws.numel(), stream.cuda_stream), f"orth({K}x{r})")
+    return Q

@@ -1,0 +1,316 @@
+// C ABI of libspanqr: argument checks, workspace layout and the orth pass sequence.
+//
+// orth(X) (candidates/kcholqr.py:112-132, kcholqr_f with eps 5e-7, alpha 1e-7, tau 1e-8, ns 2) as a stream-ordered
+// sequence of kernels; no host synchronisation, no device allocation.  Between passes Y lives in Q (the row-block
+// kernels run in place), so the workspace holds only r x r matrices and the Gram partials.
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "../../include/spanqr.h"
+#include "kernels.h"
+
+using namespace spq;
+
+namespace {
+
+constexpr float EPS = 5e-7f;    // dust weight, pass 1 (kcholqr.py:112)
+constexpr int NS_STEPS = 2;     // Newton-Schulz polish steps (kcholqr.py:112)
+constexpr int PASSES = 3;       // shifted Cholesky-QR passes (kcholqr.py:125)
+
+thread_local char g_cuda_err[256] = "";
+
+int cuda_fail(cudaError_t e) {
+    std::snprintf(g_cuda_err, sizeof(g_cuda_err), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+    return SPANQR_ERR_CUDA;
+}
+
+// ---- optional per-kernel timing (spanqr_timing_*) ----
+enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM, K_NS, K_COUNT };
+const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_partial", "k_gram_reduce", "k_rowsq",
+                                         "k_chol", "k_trsm", "k_ns_update"};
+struct TimedLaunch {
+    int kind;
+    cudaEvent_t a, b;
+};
+thread_local bool g_timing = false;
+thread_local std::vector<TimedLaunch> g_launches;
+thread_local std::vector<cudaEvent_t> g_event_pool;
+
+cudaEvent_t pooled_event() {
+    if (!g_event_pool.empty()) {
+        cudaEvent_t e = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    return e;
+}
+
+// run `launch` bracketed by events when timing is on
+template <typename F>
+cudaError_t timed(int kind, cudaStream_t st, F&& launch) {
+    if (!g_timing) return launch();
+    TimedLaunch t{kind, pooled_event(), pooled_event()};
+    if (!t.a || !t.b) return launch();
+    cudaEventRecord(t.a, st);
+    const cudaError_t e = launch();
+    cudaEventRecord(t.b, st);
+    g_launches.push_back(t);
+    return e;
+}
+
+size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Layout {
+    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, P, total;
+};
+
+Layout layout(int K, int r, int B) {
+    const GramPlan gp = gram_plan(K, r);
+    Layout l;
+    size_t o = 0;
+    l.status = o;  o += al256(256);
+    l.ptrs = o;    o += al256(sizeof(MatPtr) * (size_t)B);
+    l.maxbits = o; o += al256(sizeof(uint32_t) * (size_t)B);
+    l.scal = o;    o += al256(sizeof(PassScal) * (size_t)B * PASSES);
+    l.rowsq = o;   o += al256(sizeof(double) * (size_t)B * r);
+    l.G = o;       o += al256(sizeof(float) * (size_t)B * r * r);
+    l.L = o;       o += al256(sizeof(float) * (size_t)B * r * r);
+    l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
+    l.P = o;       o += al256(sizeof(float) * (size_t)B * gp.S * gp.tiles * GT * GT);
+    l.total = o;
+    return l;
+}
+
+bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_shape(int K, int r, int B) {
+    if (r < TB || r > MAX_R || r % TB != 0 || K < r || B < 1 || B > 65535) return SPANQR_ERR_SHAPE;
+    if ((long long)K * r > (1LL << 31)) return SPANQR_ERR_SHAPE;
+    return SPANQR_OK;
+}
+
+int check_ws(void* ws, size_t ws_bytes, int K, int r, int B) {
+    if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return SPANQR_ERR_WORKSPACE;
+    if (ws_bytes < layout(K, r, B).total) return SPANQR_ERR_WORKSPACE;
+    return SPANQR_OK;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
+
+// The pass sequence of kcholqr_f for B matrices whose pointers are in the workspace table (filled by k_setup_*).
+int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, void* ws, cudaStream_t st) {
+    const Layout l = layout(K, r, B);
+    const GramPlan gp = gram_plan(K, r);
+    PtrArg p{at<MatPtr>(ws, l.ptrs), MatPtr{nullptr, nullptr}};
+    uint32_t* maxbits = at<uint32_t>(ws, l.maxbits);
+    PassScal* scal = at<PassScal>(ws, l.scal);
+    double* rowsq = at<double>(ws, l.rowsq);
+    float* G = at<float>(ws, l.G);
+    float* Lm = at<float>(ws, l.L);
+    float* Li = at<float>(ws, l.Li);
+    float* P = at<float>(ws, l.P);
+    cudaError_t e;
+#define SPQ_TRY(call)                          \
+    do {                                       \
+        if ((e = (call)) != cudaSuccess) return cuda_fail(e); \
+    } while (0)
+    SPQ_TRY(timed(K_ABSMAX, st, [&] { return launch_absmax(p, K, r, ldx, B, maxbits, st); }));
+    for (int pass = 0; pass < PASSES; ++pass) {
+        const bool first = pass == 0;
+        const ScaleArg sc = first ? ScaleArg{maxbits, nullptr} : ScaleArg{nullptr, nullptr};
+        SPQ_TRY(timed(K_GRAM, st, [&] {
+            return launch_gram_partial(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, P, st);
+        }));
+        SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 0, G, st); }));
+        SPQ_TRY(timed(K_ROWSQ, st, [&] { return launch_rowsq(G, r, B, rowsq, st); }));
+        SPQ_TRY(timed(K_CHOL, st, [&] {
+            return launch_chol(G, Lm, Li, r, B, rowsq, nullptr, scal + (size_t)pass * B, 0, st);
+        }));
+        SPQ_TRY(timed(K_TRSM, st, [&] {
+            return launch_trsm(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
+                               first ? EPS : 0.0f, Lm, Li, st);
+        }));
+    }
+    for (int it = 0; it < NS_STEPS; ++it) {
+        SPQ_TRY(timed(K_GRAM, st, [&] {
+            return launch_gram_partial(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, P, st);
+        }));
+        SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, st); }));
+        SPQ_TRY(timed(K_NS, st, [&] { return launch_ns_update(p, K, r, ldq, B, G, st); }));
+    }
+#undef SPQ_TRY
+    return SPANQR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int spanqr_version(void) { return 100; }
+
+const char* spanqr_strerror(int code) {
+    switch (code) {
+        case SPANQR_OK: return "ok";
+        case SPANQR_ERR_SHAPE: return "unsupported shape (r must be a multiple of 32 in [32, 512], K >= r, 1 <= batch <= 65535)";
+        case SPANQR_ERR_ARG: return "bad argument (null or not 16-byte aligned pointer, or bad leading dimension)";
+        case SPANQR_ERR_WORKSPACE: return "workspace too small or not 256-byte aligned";
+        case SPANQR_ERR_CUDA: return "CUDA error";
+        case SPANQR_ERR_DEVICE: return "device reported a failure";
+        default: return "unknown status";
+    }
+}
+
+const char* spanqr_last_cuda_error(void) { return g_cuda_err; }
+
+int spanqr_workspace_bytes(int K, int r, int batch, size_t* bytes) {
+    if (!bytes) return SPANQR_ERR_ARG;
+    const int rc = check_shape(K, r, batch);
+    if (rc) return rc;
+    *bytes = layout(K, r, batch).total;
+    return SPANQR_OK;
+}
+
+int spanqr_orth_strided_f32(const float* X, long long ldx, long long strideX, float* Q, long long ldq,
+                            long long strideQ, int K, int r, int batch, const float* Z, void* ws, size_t ws_bytes,
+                            spanqr_stream_t stream) {
+    int rc = check_shape(K, r, batch);
+    if (rc) return rc;
+    if (!X || !Q || !Z || !a16(X) || !a16(Q) || !a16(Z)) return SPANQR_ERR_ARG;
+    if (ldx < r || ldq < r || ldx % 4 || ldq % 4) return SPANQR_ERR_ARG;
+    if (batch > 1 && (strideX % 4 || strideQ % 4 || strideQ < (long long)(K - 1) * ldq + r)) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, r, batch))) return rc;
+    const Layout l = layout(K, r, batch);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = timed(K_SETUP, st, [&] {
+        return launch_setup_strided(at<MatPtr>(ws, l.ptrs), X, strideX, Q, strideQ, batch, at<uint32_t>(ws, l.maxbits),
+                                    at<int>(ws, l.status), st);
+    });
+    if (e != cudaSuccess) return cuda_fail(e);
+    return run_orth(K, r, batch, ldx, ldq, Z, ws, st);
+}
+
+int spanqr_orth_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z, void* ws,
+                    size_t ws_bytes, spanqr_stream_t stream) {
+    return spanqr_orth_strided_f32(X, ldx, 0, Q, ldq, 0, K, r, 1, Z, ws, ws_bytes, stream);
+}
+
+int spanqr_orth_batched_f32(const float* const* dX, float* const* dQ, int K, int r, int batch, const float* Z,
+                            void* ws, size_t ws_bytes, spanqr_stream_t stream) {
+    int rc = check_shape(K, r, batch);
+    if (rc) return rc;
+    if (!dX || !dQ || !Z || !a16(Z)) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, r, batch))) return rc;
+    const Layout l = layout(K, r, batch);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = timed(K_SETUP, st, [&] {
+        return launch_setup_array(at<MatPtr>(ws, l.ptrs), dX, dQ, batch, at<uint32_t>(ws, l.maxbits),
+                                  at<int>(ws, l.status), st);
+    });
+    if (e != cudaSuccess) return cuda_fail(e);
+    return run_orth(K, r, batch, r, r, Z, ws, st);
+}
+
+int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r, int batch, const float* Z, void* ws,
+                         size_t ws_bytes, spanqr_stream_t stream) {
+    int rc = check_shape(K, r, batch);
+    if (rc) return rc;
+    if (!hX || !hQ || !Z || !a16(Z)) return SPANQR_ERR_ARG;
+    for (int b = 0; b < batch; ++b)
+        if (!hX[b] || !hQ[b] || !a16(hX[b]) || !a16(hQ[b])) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, r, batch))) return rc;
+    const Layout l = layout(K, r, batch);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = timed(K_SETUP, st, [&] {
+        return launch_setup_host(at<MatPtr>(ws, l.ptrs), hX, hQ, batch, at<uint32_t>(ws, l.maxbits),
+                                 at<int>(ws, l.status), st);
+    });
+    if (e != cudaSuccess) return cuda_fail(e);
+    return run_orth(K, r, batch, r, r, Z, ws, st);
+}
+
+int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_s, float* G, void* ws,
+                    size_t ws_bytes, spanqr_stream_t stream) {
+    int rc = check_shape(K, n, 1);
+    if (rc) return rc;
+    if (!Y || !G || !a16(Y) || ldy < n || ldy % 4) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, n, 1))) return rc;
+    const Layout l = layout(K, n, 1);
+    const GramPlan gp = gram_plan(K, n);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    PtrArg p{nullptr, MatPtr{Y, nullptr}};
+    cudaError_t e = launch_gram_partial(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, at<float>(ws, l.P), st);
+    if (e == cudaSuccess) e = launch_gram_reduce(at<float>(ws, l.P), n, 1, gp, 0, G, st);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_chol_f32(const float* G, int n, const float* d_tau, float* L, float* Li, void* ws, size_t ws_bytes,
+                    spanqr_stream_t stream) {
+    int rc = check_shape(n, n, 1);
+    if (rc) return rc;
+    if (!G || !d_tau || !L || !Li) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, n, n, 1))) return rc;
+    const Layout l = layout(n, n, 1);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* A = at<float>(ws, l.G);
+    cudaError_t e = cudaMemcpyAsync(A, G, sizeof(float) * (size_t)n * n, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = launch_chol(A, L, Li, n, 1, nullptr, d_tau, nullptr, 1, st);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* d_s, float eps, const float* L,
+                    const float* Li, int K, int n, float* Y, long long ldy, spanqr_stream_t stream) {
+    int rc = check_shape(K, n, 1);
+    if (rc) return rc;
+    if (!X || !Y || !L || !Li || !a16(X) || !a16(Y) || (Z && !a16(Z))) return SPANQR_ERR_ARG;
+    if (ldx < n || ldy < n || ldx % 4 || ldy % 4) return SPANQR_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    PtrArg p{nullptr, MatPtr{X, Y}};
+    cudaError_t e = launch_trsm(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li, st);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_timing_enable(int on) {
+    g_timing = on != 0;
+    return SPANQR_OK;
+}
+
+int spanqr_timing_collect(double* ms, long long* launches, int nkinds) {
+    if ((!ms || !launches) && nkinds > 0) return SPANQR_ERR_ARG;
+    int rc = SPANQR_OK;
+    for (const TimedLaunch& t : g_launches) {
+        float dt = 0.0f;
+        cudaError_t e = cudaEventSynchronize(t.b);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&dt, t.a, t.b);
+        if (e != cudaSuccess) rc = cuda_fail(e);
+        else if (t.kind < nkinds) {
+            ms[t.kind] += dt;
+            launches[t.kind] += 1;
+        }
+        g_event_pool.push_back(t.a);
+        g_event_pool.push_back(t.b);
+    }
+    g_launches.clear();
+    return rc;
+}
+
+int spanqr_kernel_kinds(void) { return K_COUNT; }
+
+const char* spanqr_kernel_kind_name(int kind) { return (kind >= 0 && kind < K_COUNT) ? KIND_NAMES[kind] : ""; }
+
+int spanqr_read_status(const void* ws, spanqr_stream_t stream, int* device_status) {
+    if (!ws || !device_status) return SPANQR_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, ws, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *device_status = h;
+    return h ? SPANQR_ERR_DEVICE : SPANQR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,64 @@
+// Host-side launchers of the spanqr kernels (one translation unit per kernel family).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace spq {
+
+// Source of a kernel's input matrix: the caller's X, or the in-progress Q (which holds Y between passes).
+enum Src : int { SRC_X = 0, SRC_Q = 1 };
+
+// Pointer source for a kernel: a device table of per-matrix pointers, or (when tab is null) one pair by value.
+struct PtrArg {
+    const MatPtr* tab;
+    MatPtr one;
+};
+
+// The scale applied on load: pow2_scale(max |X|) from the absmax bits, an explicit device scalar per matrix, or 1.
+struct ScaleArg {
+    const uint32_t* maxbits;  // [B] or null
+    const float* s;           // [B] or null
+};
+
+// Split-K plan of the compensated Gram (candidates/tri.py:365-370 at 148 SMs, tiles of 64, chunks of 32 rows).
+struct GramPlan {
+    int nt;      // tiles per side, n / 64 rounded up
+    int tiles;   // upper tiles nt (nt + 1) / 2
+    int S;       // splits
+    int KS;      // rows per split (a multiple of 32)
+};
+GramPlan gram_plan(int K, int n);
+
+cudaError_t launch_setup_strided(MatPtr* tab, const float* X, long long sX, float* Q, long long sQ, int B,
+                                 uint32_t* maxbits, int* status, cudaStream_t st);
+cudaError_t launch_setup_array(MatPtr* tab, const float* const* dX, float* const* dQ, int B, uint32_t* maxbits,
+                               int* status, cudaStream_t st);
+// host arrays of pointers, passed by value to the set-up kernel in chunks
+cudaError_t launch_setup_host(MatPtr* tab, const float* const* hX, float* const* hQ, int B, uint32_t* maxbits,
+                              int* status, cudaStream_t st);
+cudaError_t launch_absmax(PtrArg p, int K, int r, long long ldx, int B, uint32_t* maxbits, cudaStream_t st);
+
+// partial Grams P[b][split][tile][64][64] of the source matrix (ld) scaled as `sc`
+cudaError_t launch_gram_partial(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
+                                float* P, cudaStream_t st);
+// G[b] (n x n, both triangles) = fp64 sum over splits; with make_D, D = 0.5 (I - G) instead
+cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G,
+                               cudaStream_t st);
+// rowsq[b][a] = sum_c G[b][a][c]^2 in fp64, columns in order
+cudaError_t launch_rowsq(const float* G, int n, int B, double* rowsq, cudaStream_t st);
+
+// Clamped Cholesky of A[b] (n x n, lower tiles read, overwritten).  Pipeline mode (rowsq != null): nrm from rowsq,
+// A_ii += 1e-7 nrm, tau = 1e-8 nrm + 1e-30, scalars to scal[b].  Component mode: tau = *tau_ptr, no shift.
+cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, const float* tau_ptr,
+                        PassScal* scal, int zero_upper, cudaStream_t st);
+
+// Y = (s X + eps Z) L^-T per matrix: input from `src`, output to Q (in place when src == SRC_Q)
+cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
+                        ScaleArg sc, float eps, const float* L, const float* Li, cudaStream_t st);
+
+// Q <- Q + Q D per matrix, in place (D symmetric, n x n per matrix)
+cudaError_t launch_ns_update(PtrArg p, int K, int n, long long ldq, int B, const float* D, cudaStream_t st);
+
+}  // namespace spq

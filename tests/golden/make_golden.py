@@ -135,6 +135,24 @@ def main():
     np.savez_compressed(a.out, **out)
     print("wrote", a.out, os.path.getsize(a.out), "bytes")
 
+    # fingerprints of the reference generator's matrices (tests/cases.py must reproduce them) and the reference's
+    # published per-case metrics (results/synth_kcholf.json, results/synth_kcholf_rtx5060ti.json)
+    import json
+    fps = {}
+    for K, r in [(768, 512), (2048, 512), (3584, 256), (5120, 256), (17408, 256)]:
+        for c in gen.make_cases(K, r, None, (0,)):
+            fps[f"{K}x{r}/{c.name}"] = hashlib.sha1(c.X.numpy().tobytes()).hexdigest()[:16]
+    pub = {}
+    for fn in ("synth_kcholf.json", "synth_kcholf_rtx5060ti.json"):
+        d = json.load(open(os.path.join(a.ref, "results", fn)))
+        pub[fn] = {"device": d["device"],
+                   "rows": [{k: w[k] for k in ("K", "r", "case", "hard", "cond", "orth", "span_n", "hh_span_n", "fails")}
+                            for w in d["rows"]]}
+    side = os.path.join(os.path.dirname(a.out), "reference_fixtures.json")
+    with open(side, "w") as f:
+        json.dump({"gen_fingerprints": fps, "published": pub}, f, indent=0, sort_keys=True)
+    print("wrote", side, os.path.getsize(side), "bytes")
+
 
 if __name__ == "__main__":
     main()

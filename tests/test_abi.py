@@ -1,0 +1,68 @@
+"""The C ABI without a GPU: libspanqr.so loads, exports every entry point include/spanqr.h declares, and rejects bad
+arguments with the documented status codes before touching the device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from spanqr_b200 import _lib
+
+HDR = Path(__file__).resolve().parent.parent / "include" / "spanqr.h"
+OK, SHAPE, ARG, WS = 0, 1, 2, 3
+
+
+def declared():
+    text = re.sub(r"/\*.*?\*/", "", HDR.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(spanqr_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_exports_every_declared_symbol():
+    L = _lib.lib()
+    names = declared()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), "the ctypes table must bind exactly the declared entry points"
+
+
+def test_version_and_strerror():
+    L = _lib.lib()
+    assert L.spanqr_version() >= 100
+    for c in range(6):
+        assert L.spanqr_strerror(c)
+    assert L.spanqr_last_cuda_error() is not None
+
+
+@pytest.mark.parametrize("K,r,B,rc", [(768, 512, 1, OK), (17408, 256, 1, OK), (3584, 256, 96, OK), (100, 96, 1, OK),
+                                      (768, 100, 1, SHAPE), (768, 544, 1, SHAPE), (100, 128, 1, SHAPE),
+                                      (768, 0, 1, SHAPE), (768, 512, 0, SHAPE)])
+def test_workspace_bytes(K, r, B, rc):
+    n = ctypes.c_size_t(0)
+    assert _lib.lib().spanqr_workspace_bytes(K, r, B, ctypes.byref(n)) == rc
+    if rc == OK:
+        assert n.value > 4 * r * r * B
+
+
+def test_argument_checks_before_any_device_work():
+    L = _lib.lib()
+    ws_need = _lib.workspace_bytes(256, 64, 1)
+    fake = 1 << 20                 # never dereferenced: every call below fails its checks first
+    al = fake * 256
+    assert L.spanqr_orth_f32(al, 64, al, 64, 256, 100, al, al, ws_need, None) == SHAPE
+    assert L.spanqr_orth_f32(None, 64, al, 64, 256, 64, al, al, ws_need, None) == ARG
+    assert L.spanqr_orth_f32(al + 4, 64, al, 64, 256, 64, al, al, ws_need, None) == ARG     # misaligned X
+    assert L.spanqr_orth_f32(al, 62, al, 64, 256, 64, al, al, ws_need, None) == ARG         # ldx < r
+    assert L.spanqr_orth_f32(al, 64, al, 64, 256, 64, al, al, ws_need - 1, None) == WS      # workspace too small
+    assert L.spanqr_orth_f32(al, 64, al, 64, 256, 64, al, al + 16, ws_need, None) == WS     # workspace misaligned
+    assert L.spanqr_orth_strided_f32(al, 64, 64 * 256, al, 64, 10, 256, 64, 2, al, al, 10 ** 9, None) == ARG  # overlap
+    assert L.spanqr_chol_f32(al, 100, al, al, al, al, 10 ** 9, None) == SHAPE
+    assert L.spanqr_trsm_f32(al, 64, None, None, 0.0, al, al, 256, 64, al, 60, None) == ARG
+    assert L.spanqr_gram_f32(al, 64, 32, 64, None, al, al, 10 ** 9, None) == SHAPE           # K < n
+    st = ctypes.c_int(7)
+    assert L.spanqr_read_status(None, None, ctypes.byref(st)) == ARG
+
+
+def test_error_type_names_the_code():
+    with pytest.raises(_lib.SpanqrError, match="unsupported shape"):
+        _lib.check(SHAPE, "orth")

@@ -1,0 +1,77 @@
+"""Each CUDA kernel family against the oracle, through the C ABI.
+
+The clamped Cholesky (k_chol) evaluates exactly the oracle's operation sequence (chol.cu's), so its L and Li must
+equal the oracle's bit for bit.  The split Gram and the row-block solve are held to the same bar while they run the
+oracle's order; the golden Gram is the reference's own gram_f output."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from tests import gpu_util as gu
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def spd(n, K, seed, shift_rel=1e-7):
+    rng = np.random.default_rng(seed)
+    M = rng.standard_normal((K, n)).astype(np.float32) * np.logspace(0, -3, n).astype(np.float32)
+    G = oracle.gram_kahan(M)
+    nrm = oracle.fro(G)
+    G[np.diag_indices(n)] += np.float32(np.float32(shift_rel) * nrm)
+    return G, np.float32(np.float32(np.float32(1e-8) * nrm) + np.float32(1e-30))
+
+
+@pytest.mark.parametrize("n", [32, 64, 96, 128, 256, 512])
+def test_chol_bitwise(n):
+    G, tau = spd(n, 3 * n, n)
+    L, Li = gu.chol(G, tau)
+    Lo, Lio = oracle.chol32(G, tau)
+    assert gu.bits_equal(L, Lo) and gu.bits_equal(Li, Lio)
+
+
+def test_chol_bitwise_golden_and_clamped():
+    g = np.load(GOLD / "golden.npz")
+    L, Li = gu.chol(g["comp/Gs"], g["comp/tau"][0])
+    assert gu.bits_equal(L, g["comp/L"]) and gu.bits_equal(Li, g["comp/Li"])
+    Z = np.zeros((128, 128), np.float32)                       # every pivot clamped
+    L, Li = gu.chol(Z, 1e-6)
+    Lo, Lio = oracle.chol32(Z, 1e-6)
+    assert gu.bits_equal(L, Lo) and gu.bits_equal(Li, Lio)
+    rng = np.random.default_rng(5)                              # rank-deficient Gram: some pivots clamped
+    M = rng.standard_normal((300, 20)).astype(np.float32) @ rng.standard_normal((20, 256)).astype(np.float32)
+    G = oracle.gram_kahan(M)
+    tau = np.float32(1e-8 * oracle.fro(G))
+    L, Li = gu.chol(G, tau)
+    Lo, Lio = oracle.chol32(G, tau)
+    assert gu.bits_equal(L, Lo) and gu.bits_equal(Li, Lio)
+
+
+@pytest.mark.parametrize("K,n,scaled", [(100, 64, False), (777, 96, True), (3584, 256, True), (2048, 512, False),
+                                        (17408, 256, False)])
+def test_gram_bitwise(K, n, scaled):
+    rng = np.random.default_rng(K + n)
+    Y = (rng.standard_normal((K, n)) * 3.0).astype(np.float32)
+    s = 0.25 if scaled else None
+    assert gu.bits_equal(gu.gram(Y, s), oracle.gram_kahan(Y, s=s))
+
+
+def test_gram_equals_reference_gram_f():
+    """the golden G0 is the reference's own tri.gram_f(X, s) (run by Triton's interpreter)"""
+    g = np.load(GOLD / "golden.npz")
+    assert gu.bits_equal(gu.gram(g["comp/X"], float(g["comp/s"][0])), g["comp/G0"])
+
+
+@pytest.mark.parametrize("K,n", [(100, 64), (1000, 256), (777, 512)])
+def test_trsm_bitwise(K, n):
+    rng = np.random.default_rng(K * n)
+    X = rng.standard_normal((K, n)).astype(np.float32)
+    G, tau = spd(n, 2 * n, K)
+    L, Li = oracle.chol32(G, tau)
+    Z = oracle.dust(K, n)
+    Y = gu.trsm(X, L, Li, s=0.5, Z=Z, eps=5e-7)
+    assert gu.bits_equal(Y, oracle.trsm(X, L, Li, s=0.5, Z=Z, eps=5e-7))
+    Y2 = gu.trsm(X, L, Li, inplace=True)
+    assert gu.bits_equal(Y2, oracle.trsm(X, L, Li))

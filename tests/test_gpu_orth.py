@@ -1,0 +1,106 @@
+"""orth on the GPU: against the oracle, against the reference's own outputs (golden vectors), against the reference's
+pass criteria at the TTF shapes, and the hygiene rules (deterministic, no host sync, input untouched)."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from spanqr_b200 import orth, zdust
+from tests import cases, metrics
+from tests import gpu_util as gu
+from tests.test_oracle import elementwise_tol, _kappa
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+PUB = json.loads((GOLD / "reference_fixtures.json").read_text())["published"]["synth_kcholf.json"]["rows"]
+PUB = {(w["K"], w["r"], w["case"]): w for w in PUB}
+
+
+def test_orth_golden_equals_oracle_bitwise():
+    g = np.load(GOLD / "golden.npz")
+    for key in g["names"]:
+        key = str(key)
+        K, r = map(int, key.split("/")[0].split("x"))
+        X, Z = g["X/" + key], oracle.dust(K, r)
+        assert gu.bits_equal(gu.orth_with_dust(X, Z), oracle.orth(X, Z)), key
+
+
+def test_orth_golden_vs_reference_outputs():
+    """the reference's kcholqr_f outputs on the same X and dust: elementwise within the kappa-dependent bound"""
+    g = np.load(GOLD / "golden.npz")
+    for key in g["names"]:
+        key = str(key)
+        K, r = map(int, key.split("/")[0].split("x"))
+        X, Qref = g["X/" + key], g["Q/" + key]
+        Q = gu.orth_with_dust(X, oracle.dust(K, r))
+        assert np.isfinite(Q).all()
+        assert np.abs(Q.astype(np.float64).T @ Q - np.eye(r)).max() <= 3e-7, key
+        k = _kappa(X)
+        if k <= 1e6:
+            assert np.abs(Q - Qref).max() <= elementwise_tol(k), key
+
+
+@pytest.mark.parametrize("shape", ["768x512", "2048x512", "5120x256"])
+def test_orth_equals_oracle_at_ttf_shape_with_cuda_dust(shape):
+    K, r = map(int, shape.split("x"))
+    X = cases.make_case(K, r, "ttf_cu4_t1e-2")
+    Z = zdust(K, r, "cuda").cpu().numpy()
+    Q = orth(X.cuda()).cpu().numpy()
+    assert gu.bits_equal(Q, oracle.orth(X.numpy(), Z))
+
+
+@pytest.mark.parametrize("shape", ["768x512", "3584x256", "17408x256"])
+def test_reference_suite_passes_at_ttf_shape(shape):
+    """every reference case: finite, no degenerate column, orth <= 2e-7, span within 2x the reference's published
+    span for that matrix (results/synth_kcholf.json) and within the harness bound of 10x Householder"""
+    K, r = map(int, shape.split("x"))
+    for name in cases.case_names(K, r):
+        X = cases.make_case(K, r, name)
+        ref = metrics.reference(X)
+        Q = orth(X.cuda())
+        ev = metrics.evaluate(Q, X, ref)
+        assert ev["finite"] and ev["bad_cols"] == 0, (name, ev)
+        assert ev["orth"] <= 2e-7, (name, ev)
+        hh = metrics.evaluate(torch.linalg.qr(X.cuda())[0], X, ref)["span_n"]
+        assert ev["span_n"] <= max(10 * hh, 100), (name, ev, hh)
+        w = PUB.get((K, r, name + "/s0"))
+        if w is not None:
+            assert ev["span_n"] <= max(2 * w["span_n"], 1.0), (name, ev["span_n"], w["span_n"])
+
+
+def test_hygiene_deterministic_sync_free_input_intact():
+    X = cases.cfg1().cuda()
+    X0 = X.clone()
+    orth(X)
+    torch.cuda.synchronize()
+    prev = torch.cuda.get_sync_debug_mode()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        Q1 = orth(X)
+        Q2 = orth(X)
+    finally:
+        torch.cuda.set_sync_debug_mode(prev)
+    torch.cuda.synchronize()
+    assert Q1.dtype == torch.float32 and Q1.is_contiguous() and Q1.shape == X.shape and Q1.device == X.device
+    assert torch.equal(Q1.view(torch.int32), Q2.view(torch.int32))
+    assert torch.equal(X.view(torch.int32), X0.view(torch.int32))
+
+
+@pytest.mark.parametrize("name,seed", [("cfg0", 0), ("cfg1", 0), ("cfg1", 1)])
+def test_baseline_configs_quality(name, seed):
+    X = (cases.cfg0(seed) if name == "cfg0" else cases.cfg1(seed))
+    ref = metrics.reference(X)
+    ev = metrics.evaluate(orth(X.cuda()), X, ref)
+    hh = metrics.evaluate(torch.linalg.qr(X.cuda())[0], X, ref)["span_n"]
+    assert ev["finite"] and ev["bad_cols"] == 0 and ev["orth"] <= 2e-7, ev
+    assert ev["span_n"] <= max(10 * hh, 100), (ev, hh)
+
+
+def test_rejects_unsupported_shapes_loudly():
+    with pytest.raises(ValueError):
+        orth(torch.zeros(100, 48, device="cuda"))
+    with pytest.raises(TypeError):
+        orth(torch.zeros(100, 64, device="cuda", dtype=torch.float64))

@@ -1,0 +1,110 @@
+"""BASELINE config 2 (robustness sweep at the 27B shapes), the exact power-of-2 scale invariance, and orth_batched:
+batch-independent bits, every batched entry point, mixed shapes, and (with 2+ GPUs) the multi-rank path over NCCL."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from spanqr_b200 import orth, orth_batched, zdust, workspace, _lib
+from tests import cases, metrics
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("K", [5120, 17408])
+def test_robustness_sweep(K):
+    for name in cases.CFG2_CASES:
+        X = cases.cfg2(K, name)
+        ev = metrics.evaluate(orth(X.cuda()), X)
+        assert ev["finite"] and ev["bad_cols"] == 0, (K, name, ev)
+        assert ev["orth"] <= 2e-7, (K, name, ev)
+        assert ev["span_n"] <= 100, (K, name, ev)
+
+
+@pytest.mark.parametrize("K", [5120, 17408])
+def test_pow2_scaling_is_exact(K):
+    """Q(2^83 X) and Q(2^-83 X) equal Q(X) bit for bit: the scale is an exact power of 2 applied on load"""
+    Q = orth(cases.cfg2(K, "base83").cuda())
+    for name in ("scale_p83", "scale_m83"):
+        assert torch.equal(orth(cases.cfg2(K, name).cuda()).view(torch.int32), Q.view(torch.int32)), name
+
+
+def _bits(a, b):
+    return torch.equal(a.contiguous().view(torch.int32), b.contiguous().view(torch.int32))
+
+
+def test_batched_equals_single_bitwise():
+    Xs = [cases.cfg3_matrix(i, K=1024).cuda() for i in range(13)]
+    single = [orth(x) for x in Xs]
+    for got in (orth_batched(Xs), list(orth_batched(torch.stack(Xs)).unbind(0))):
+        assert all(_bits(a, b) for a, b in zip(got, single))
+
+
+def test_batched_mixed_shapes():
+    Xs = [cases.cfg4_matrix(i, n_small=3, K_small=1024, K_big=2048, N=512).cuda() for i in range(5)]
+    Xs.append(cases.make_case(768, 512, "mixed_c6").cuda())
+    got = orth_batched(Xs)
+    for x, q in zip(Xs, got):
+        assert q.shape == x.shape and _bits(q, orth(x))
+
+
+def test_strided_and_device_pointer_entry_points():
+    B, K, r = 4, 512, 128
+    X = torch.stack([cases.cfg3_matrix(i, K=K, r=r) for i in range(B)]).cuda()
+    want = torch.stack([orth(X[b]) for b in range(B)])
+    Z = zdust(K, r, X.device)
+    st = torch.cuda.current_stream().cuda_stream
+    ws = workspace(X.device, K, r, B)
+    Q = torch.empty_like(X)
+    _lib.check(_lib.lib().spanqr_orth_strided_f32(X.data_ptr(), r, K * r, Q.data_ptr(), r, K * r, K, r, B,
+                                                  Z.data_ptr(), ws.data_ptr(), ws.numel(), st), "strided")
+    assert _bits(Q, want)
+    Q2 = torch.empty_like(X)
+    dX = torch.tensor([X[b].data_ptr() for b in range(B)], dtype=torch.int64, device=X.device)
+    dQ = torch.tensor([Q2[b].data_ptr() for b in range(B)], dtype=torch.int64, device=X.device)
+    _lib.check(_lib.lib().spanqr_orth_batched_f32(dX.data_ptr(), dQ.data_ptr(), K, r, B, Z.data_ptr(), ws.data_ptr(),
+                                                  ws.numel(), st), "batched")
+    assert _bits(Q2, want)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        Xs = [cases.cfg4_matrix(i, n_small=6, K_small=1024, K_big=2048, N=512).cuda() for i in range(9)]
+        Qs = orth_batched(Xs)
+        torch.cuda.synchronize()
+        q.put((rank, [x.cpu() for x in Qs]))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_multi_gpu_matches_single_gpu_bitwise():
+    import torch.multiprocessing as mp
+    Xs = [cases.cfg4_matrix(i, n_small=6, K_small=1024, K_big=2048, N=512).cuda() for i in range(9)]
+    want = [orth(x).cpu() for x in Xs]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for rank in range(2):
+        assert all(_bits(a, b) for a, b in zip(res[rank], want)), rank

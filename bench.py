@@ -208,7 +208,7 @@ def cpu_baseline(spec, budget_s=20.0):
     t = time.perf_counter()
     oracle.orth_batch(Xs, [Z] * th)
     one = time.perf_counter() - t
-    rounds = int(min(4, max(1, budget_s / max(one, 1e-3))))
+    rounds = int(min(32, max(1, budget_s / max(one, 1e-3))))
     t = time.perf_counter()
     for _ in range(rounds):
         oracle.orth_batch(Xs, [Z] * th)

@@ -72,6 +72,12 @@ def orth_with_dust(X, Z):
 
 
 def bits_equal(a, b):
-    a = np.ascontiguousarray(a, np.float32)
-    b = np.ascontiguousarray(b, np.float32)
-    return a.shape == b.shape and bool(np.array_equal(a.view(np.uint32), b.view(np.uint32)))
+    """bit-for-bit equality, every NaN counted as one value (the GPU's canonical NaN is 0x7fffffff, the CPU's
+    0x7fc00000)"""
+    a = np.ascontiguousarray(a, np.float32).view(np.uint32).copy()
+    b = np.ascontiguousarray(b, np.float32).view(np.uint32).copy()
+    if a.shape != b.shape:
+        return False
+    a[np.isnan(a.view(np.float32))] = 0x7FC00000
+    b[np.isnan(b.view(np.float32))] = 0x7FC00000
+    return bool(np.array_equal(a, b))

@@ -40,7 +40,8 @@ enum spanqr_status {
     SPANQR_ERR_ARG = 2,       /* null or misaligned pointer, leading dimension too small or not a multiple of 4 */
     SPANQR_ERR_WORKSPACE = 3, /* workspace too small or not 256-byte aligned                                    */
     SPANQR_ERR_CUDA = 4,      /* a CUDA runtime call or kernel launch failed                                    */
-    SPANQR_ERR_DEVICE = 5     /* the device status word reports a failure (spanqr_read_status)                  */
+    SPANQR_ERR_DEVICE = 5,    /* the device status word reports a failure (spanqr_read_status)                  */
+    SPANQR_ERR_TOO_LARGE = 6  /* the shape needs more scratch than spanqr_orth_noalloc_f32's fixed array holds     */
 };
 
 /* version as MAJOR * 10000 + MINOR * 100 + PATCH */
@@ -78,6 +79,21 @@ int spanqr_orth_batched_f32(const float* const* dX, float* const* dQ, int K, int
  * host-to-device copy and no pinned memory is involved; leading dimension r for all) */
 int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r, int batch, const float* Z,
                          void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * orth of one matrix for callers that cannot allocate device memory: code running inside a CUDA stream capture
+ * that must not add allocations, memory-capped sandboxes, or real-time loops that forbid cudaMalloc.  No
+ * counterpart in the reference.  Instead of a caller workspace it uses a fixed scratch array of
+ * SPANQR_NOALLOC_SCRATCH_BYTES (16 MiB) that lives in the library's device image: every GPU that loads the library
+ * holds it until the process exits.  Shapes whose spanqr_workspace_bytes(K, r, 1) exceeds it return
+ * SPANQR_ERR_TOO_LARGE.  The first call on each device looks up the array's device address (cudaGetSymbolAddress,
+ * with that device current), so make that first call before any stream capture.  All calls share the one array:
+ * calls that overlap on the GPU (other streams or threads) race and corrupt each other's results; serialise them.
+ * Nothing is allocated or freed, by this library or by any library it calls.
+ */
+#define SPANQR_NOALLOC_SCRATCH_BYTES (16u << 20)
+int spanqr_orth_noalloc_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z,
+                            spanqr_stream_t stream);
 
 /*
  * Component entry points (the reference's kernel modules), for tests and for callers that compose their own

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "../../include/spanqr.h"
@@ -161,6 +162,7 @@ const char* spanqr_strerror(int code) {
         case SPANQR_ERR_WORKSPACE: return "workspace too small or not 256-byte aligned";
         case SPANQR_ERR_CUDA: return "CUDA error";
         case SPANQR_ERR_DEVICE: return "device reported a failure";
+        case SPANQR_ERR_TOO_LARGE: return "shape needs more scratch than the no-allocation entry point's fixed 16 MiB array";
         default: return "unknown status";
     }
 }
@@ -231,6 +233,47 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
     });
     if (e != cudaSuccess) return cuda_fail(e);
     return run_orth(K, r, batch, r, r, Z, ws, st);
+}
+
+}  // extern "C"
+
+// ---- orth without any allocation: scratch in a fixed array of the device image ----
+// For callers that may not call cudaMalloc (inside a stream capture that must not add allocations, in a
+// memory-capped sandbox, in a real-time loop).  The array belongs to the library's module: each GPU that loads the
+// library keeps it until the process exits.  Its host-side name is only a stand-in, never a device address; the
+// device address is looked up once per device with cudaGetSymbolAddress and cached.
+namespace {
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SPANQR_NOALLOC_SCRATCH_BYTES];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+}  // namespace
+
+extern "C" {
+
+int spanqr_orth_noalloc_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z,
+                            spanqr_stream_t stream) {
+    int rc = check_shape(K, r, 1);
+    if (rc) return rc;
+    if (layout(K, r, 1).total > SPANQR_NOALLOC_SCRATCH_BYTES) return SPANQR_ERR_TOO_LARGE;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return SPANQR_ERR_ARG;
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> g(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // with device `dev` current
+            if (e != cudaSuccess) return cuda_fail(e);
+            g_noalloc_ptr[dev] = p;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    // the set-up kernel of the orth sequence clears the only scratch words that must start at zero (the per-matrix
+    // max |x| bits and the status word); every other scratch region is fully written before it is read
+    return spanqr_orth_f32(X, ldx, Q, ldq, K, r, Z, scratch, SPANQR_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_s, float* G, void* ws,

@@ -29,7 +29,7 @@ int cuda_fail(cudaError_t e) {
 
 // ---- optional per-kernel timing (spanqr_timing_*) ----
 enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM, K_NS, K_COUNT };
-const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_partial", "k_gram_reduce", "k_rowsq",
+const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce", "k_rowsq",
                                          "k_chol", "k_trsm", "k_ns_update"};
 struct TimedLaunch {
     int kind;
@@ -70,7 +70,7 @@ struct Layout {
 };
 
 Layout layout(int K, int r, int B) {
-    const GramPlan gp = gram_plan(K, r);
+    const GramPlan gp = gram_tc_plan(K, r);
     Layout l;
     size_t o = 0;
     l.status = o;  o += al256(256);
@@ -81,7 +81,7 @@ Layout layout(int K, int r, int B) {
     l.G = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.L = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
-    l.P = o;       o += al256(sizeof(float) * (size_t)B * gp.S * gp.tiles * GT * GT);
+    l.P = o;       o += al256(sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE);
     l.total = o;
     return l;
 }
@@ -106,8 +106,9 @@ T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws)
 // The pass sequence of kcholqr_f for B matrices whose pointers are in the workspace table (filled by k_setup_*).
 int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, void* ws, cudaStream_t st) {
     const Layout l = layout(K, r, B);
-    const GramPlan gp = gram_plan(K, r);
+    const GramPlan gp = gram_tc_plan(K, r);
     PtrArg p{at<MatPtr>(ws, l.ptrs), MatPtr{nullptr, nullptr}};
+    int* status = at<int>(ws, l.status);
     uint32_t* maxbits = at<uint32_t>(ws, l.maxbits);
     PassScal* scal = at<PassScal>(ws, l.scal);
     double* rowsq = at<double>(ws, l.rowsq);
@@ -125,7 +126,8 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         const bool first = pass == 0;
         const ScaleArg sc = first ? ScaleArg{maxbits, nullptr} : ScaleArg{nullptr, nullptr};
         SPQ_TRY(timed(K_GRAM, st, [&] {
-            return launch_gram_partial(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, P, st);
+            return launch_gram_tc(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, first ? 1 : 0, P,
+                                  status, st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 0, G, st); }));
         SPQ_TRY(timed(K_ROWSQ, st, [&] { return launch_rowsq(G, r, B, rowsq, st); }));
@@ -139,7 +141,8 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
     }
     for (int it = 0; it < NS_STEPS; ++it) {
         SPQ_TRY(timed(K_GRAM, st, [&] {
-            return launch_gram_partial(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, P, st);
+            return launch_gram_tc(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, it == NS_STEPS - 1 ? 1 : 0, P,
+                                  status, st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, st); }));
         SPQ_TRY(timed(K_NS, st, [&] { return launch_ns_update(p, K, r, ldq, B, G, st); }));
@@ -283,10 +286,13 @@ int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_
     if (!Y || !G || !a16(Y) || ldy < n || ldy % 4) return SPANQR_ERR_ARG;
     if ((rc = check_ws(ws, ws_bytes, K, n, 1))) return rc;
     const Layout l = layout(K, n, 1);
-    const GramPlan gp = gram_plan(K, n);
+    const GramPlan gp = gram_tc_plan(K, n);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     PtrArg p{nullptr, MatPtr{Y, nullptr}};
-    cudaError_t e = launch_gram_partial(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, at<float>(ws, l.P), st);
+    cudaError_t e = cudaMemsetAsync(at<int>(ws, l.status), 0, sizeof(int), st);
+    if (e == cudaSuccess)
+        e = launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, 1, at<float>(ws, l.P),
+                           at<int>(ws, l.status), st);
     if (e == cudaSuccess) e = launch_gram_reduce(at<float>(ws, l.P), n, 1, gp, 0, G, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }

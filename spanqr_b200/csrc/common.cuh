@@ -6,9 +6,7 @@
 namespace spq {
 
 constexpr int TB = 32;        // Cholesky / triangular-solve tile width (candidates/kchol.py:9 TB = 32)
-constexpr int GT = 64;        // split-Gram output tile (candidates/kcholqr.py:20, 126: bt = 64)
-constexpr int GK = 32;        // split-Gram row chunk of the compensated sum (candidates/tri.py: bk = 32)
-constexpr int NSM_SPLIT = 148;  // SM count the Gram split count is derived from (a B200; fixed, not queried)
+constexpr int GRAM_TILE = 128;  // Gram output tile (tcgen05 M = N = 128)
 constexpr int MAX_R = 512;
 
 // Per-matrix device pointers of one call (filled by k_setup_*).

@@ -1,0 +1,281 @@
+// Gram G = A^T A (A = s Y, Y [K, n] fp32 row-major) on the 5th-generation tensor cores, split-TF32 (3xTF32).
+//
+// One CTA = one 128 x 128 tile (ti <= tj) of the upper triangle of G over one 512-row split of Y.  Per 32-row chunk:
+// the 256 threads load the two 32 x 128 column panels (coalesced 32-byte row segments), split every value into
+// tf32 parts and store them K-major into 128B-swizzled shared tiles (the Gram contracts over the rows of Y, so this
+// is the transpose the MMA wants); one thread then issues, per k-step of 8 rows, tcgen05.mma M128 N128 K8 products:
+//   plain mode    (x = hi + lo, 22 of 24 bits): hi.hi | hi.lo + lo.hi                                   (3 MMAs)
+//   accurate mode (x = hi + mid + lo exactly):  hi.hi | hi.mid + mid.hi + hi.lo + mid.mid + lo.hi      (6 MMAs)
+// hi.hi goes to one TMEM accumulator and the small products to a second one, so the small terms never round
+// against the large partial sum.  After every group of rows the large-term accumulator is drained into fp64 registers
+// while the next group accumulates in the other TMEM buffer; the small-term accumulator (about 2^-11 of the total) stays in
+// TMEM for the whole split and is drained once at the end.  The split's fp64 sum is rounded to fp32 and written as
+// a partial.  k_gram_reduce (k_gram.cu) sums the partials in split order in fp64.  The accurate mode serves the two
+// Grams the reference computes with its compensated kernel (pass 1 and the last polish step, kcholqr.py:20, 126).
+// Determinism: the split size (512 rows) and every order depend only on (K, n), never on the batch or the GPU.
+// Compensation: the reference (candidates/tri.py:255-375) Kahan-sums fp32 32-row dots inside a split and adds the
+// splits in fp64; here each group of rows (32 in the accurate mode, 128 in the plain mode) sums its products in the
+// tensor core's fp32 and the groups are added in fp64.
+// The tensor core's fp32 accumulation rounds toward zero, so a sum of same-sign products drifts low by about half
+// an ulp per accumulation (measured: -19 ulps of sum |y_i y_j| after 128 rows on the diagonal, under 2.3 ulps off the
+// diagonal of an orthonormal Y).  The diagonal -- every column's sum of squares, the entries that set the final
+// orthogonality -- is therefore computed on the CUDA cores in fp64 from the same scaled values (exact squares,
+// fixed-order sums) by the diagonal-tile CTAs and written over the tensor-core diagonal.
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace spq {
+
+namespace {
+constexpr int TILE = 128;
+constexpr int CHUNK = 32;
+constexpr int OPND = 16384;     // one 128 x 32 tf32 operand tile
+constexpr int ERR_TIMEOUT = 0x10;
+// per buffer: A parts then B parts (PARTS = 2: hi, lo; PARTS = 3: hi, mid, lo)
+template <int PARTS> constexpr int buf_bytes() { return 2 * PARTS * OPND; }
+template <int PARTS> constexpr int smem_bytes() { return 2 * buf_bytes<PARTS>() + 1024 /*barriers*/ + 1024 /*alignment*/; }
+constexpr uint32_t TMEM_COLS = 512;  // large-term accumulators at 0 and 128 (two groups), small-term at 256
+}  // namespace
+
+GramPlan gram_tc_plan(int K, int n) {
+    GramPlan g;
+    g.nt = (n + TILE - 1) / TILE;
+    g.tiles = g.nt * (g.nt + 1) / 2;
+    g.KS = GRAM_TC_SPLIT;
+    g.S = (K + g.KS - 1) / g.KS;
+    return g;
+}
+
+constexpr int NT = 256;         // 8 warps: 4 TMEM lane quadrants x 2 column halves of the 128 x 128 tile
+
+template <int PARTS>
+__global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int n, long long ld, GramPlan gp,
+                                                    ScaleArg sc, float* __restrict__ P, int* __restrict__ status) {
+    // chunks per fp64 drain of the large-term accumulator: every 32 rows in the accurate mode (the truncated fp32
+    // accumulation of same-sign products then spans 4 MMAs), every 128 rows in the plain mode
+    constexpr int GROUP = (PARTS == 3) ? 1 : 4;
+    constexpr int BUF = buf_bytes<PARTS>();
+    constexpr int BOFF = PARTS * OPND;   // B parts follow the A parts
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    char* const buf0 = reinterpret_cast<char*>(sm);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 2 * BUF);   // [0,1] operand buffer free, [2,3] accumulator full
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + 2 * BUF + 64);
+
+    const int tile = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+    int ti, tj;
+    upper_tile(tile, gp.nt, ti, tj);
+    const bool diag = ti == tj;
+    const MatPtr mp = p.tab ? p.tab[b] : p.one;
+    const float* __restrict__ Y = (src == SRC_X) ? mp.X : mp.Q;
+    float s = 1.0f;
+    bool scaled = false;
+    if (sc.maxbits) {
+        s = pow2_scale(__uint_as_float(sc.maxbits[b]));
+        scaled = true;
+    } else if (sc.s) {
+        s = sc.s[b];
+        scaled = true;
+    }
+    const int k0 = sp * gp.KS;
+    const int k1 = min(k0 + gp.KS, K);
+    const int nchunks = (k1 - k0 + CHUNK - 1) / CHUNK;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (warp == 0) tc::tmem_alloc(tmem_slot, TMEM_COLS);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 4; ++i) tc::mbar_init(&bars[i], 1);
+        tc::mbar_fence_init();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    // this thread's four (row m, k-quad q) slots of a 32 x 128 panel: warps 0-3 take k-quads 0-3, warps 4-7 4-7;
+    // inside a warp 8 consecutive m (one swizzle atom) x 4 k-quads, so the 16-byte stores hit distinct banks
+    const int q = (warp >> 2) * 4 + (lane >> 3);
+    int mrow[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mrow[j] = 8 * ((warp & 3) * 4 + j) + (lane & 7);
+    const int colA = ti * TILE, colB = tj * TILE;
+
+    auto load = [&](int c, float (&ra)[16], float (&rb)[16]) {
+        const int row0 = k0 + c * CHUNK + 4 * q;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = row0 + i;
+            const bool rin = row < k1;
+            const float* yr = Y + (long long)row * ld;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float va = 0.0f, vb = 0.0f;
+                if (rin && colA + mrow[j] < n) va = __ldg(yr + colA + mrow[j]);
+                if (rin && !diag && colB + mrow[j] < n) vb = __ldg(yr + colB + mrow[j]);
+                ra[j * 4 + i] = scaled ? __fmul_rn(va, s) : va;
+                rb[j * 4 + i] = scaled ? __fmul_rn(vb, s) : vb;
+            }
+        }
+    };
+    double dsq[4] = {0.0, 0.0, 0.0, 0.0};   // diagonal tiles: sum of squares of column colA + mrow[j]
+    auto stage = [&](int bi, const float (&ra)[16], const float (&rb)[16]) {
+        char* base = buf0 + bi * BUF;
+        if (diag) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dsq[j] = __fma_rn((double)ra[j * 4 + i], (double)ra[j * 4 + i], dsq[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 v = make_float4(ra[j * 4], ra[j * 4 + 1], ra[j * 4 + 2], ra[j * 4 + 3]);
+            if constexpr (PARTS == 2) tc::store_split4(base, base + OPND, mrow[j], q, v);
+            else tc::store_split4x3(base, base + OPND, base + 2 * OPND, mrow[j], q, v);
+        }
+        if (!diag) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 v = make_float4(rb[j * 4], rb[j * 4 + 1], rb[j * 4 + 2], rb[j * 4 + 3]);
+                if constexpr (PARTS == 2) tc::store_split4(base + BOFF, base + BOFF + OPND, mrow[j], q, v);
+                else tc::store_split4x3(base + BOFF, base + BOFF + OPND, base + BOFF + 2 * OPND, mrow[j], q, v);
+            }
+        }
+    };
+
+    double acc[64];   // rows (warp & 3) * 32 + lane, columns (warp >> 2) * 64 .. + 64
+#pragma unroll
+    for (int i = 0; i < 64; ++i) acc[i] = 0.0;
+    const uint32_t idesc = tc::idesc_tf32(TILE, TILE);
+    const uint32_t tq = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * 64);
+    const uint32_t tsmall = tmem + 2 * TILE;
+
+    // add 64 accumulator columns at TMEM address t (this thread's lane) into acc
+    auto add_cols = [&](uint32_t t) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float v[32];
+            tc::tmem_ld32(t + 32 * h, v);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[32 * h + i] = __dadd_rn(acc[32 * h + i], (double)v[i]);
+        }
+    };
+    auto drain = [&](int g, bool last) -> bool {
+        const int gb = g & 1;
+        bool ok = tc::mbar_wait(&bars[2 + gb], (uint32_t)((g >> 1) & 1));
+        ok = __syncthreads_and(ok);
+        if (!ok) return false;
+        tc::fence_after_sync();
+        add_cols(tq + gb * TILE);
+        if (last) add_cols(tq + 2 * TILE);   // this thread's lanes and columns of the small-term accumulator
+        tc::fence_before_sync();
+        return true;
+    };
+
+    auto chunk = [&](int c, float (&ra)[16], float (&rb)[16]) -> bool {
+        const int bi = c & 1;
+        bool ok = true;
+        if (c >= 2) ok = tc::mbar_wait(&bars[bi], (uint32_t)(((c - 2) >> 1) & 1));
+        ok = __syncthreads_and(ok);
+        if (!ok) return false;
+        stage(bi, ra, rb);
+        tc::fence_async_smem();
+        if (c + 2 < nchunks) load(c + 2, ra, rb);
+        __syncthreads();
+        const int g = c / GROUP;
+        if (threadIdx.x == 0) {
+            tc::fence_after_sync();
+            const uint32_t abase = tc::smem_u32(buf0 + bi * BUF);
+            const uint32_t bbase = diag ? abase : abase + BOFF;
+            const uint32_t dbig = tmem + (uint32_t)((g & 1) * TILE), dsmall = tsmall;
+#pragma unroll 1
+            for (int k = 0; k < CHUNK / 8; ++k) {
+                const uint32_t acc_in = (c % GROUP != 0 || k > 0) ? 1u : 0u;          // large: per group
+                const uint32_t acc_small = (c != 0 || k > 0) ? 1u : 0u;              // small: whole split
+                const uint64_t ahi = tc::sdesc_k128(abase + 32 * k), alo = tc::sdesc_k128(abase + (PARTS - 1) * OPND + 32 * k);
+                const uint64_t bhi = tc::sdesc_k128(bbase + 32 * k), blo = tc::sdesc_k128(bbase + (PARTS - 1) * OPND + 32 * k);
+                tc::mma_tf32(dbig, ahi, bhi, idesc, acc_in);
+                if constexpr (PARTS == 2) {
+                    tc::mma_tf32(dsmall, ahi, blo, idesc, acc_small);
+                    tc::mma_tf32(dsmall, alo, bhi, idesc, 1u);
+                } else {
+                    const uint64_t amid = tc::sdesc_k128(abase + OPND + 32 * k), bmid = tc::sdesc_k128(bbase + OPND + 32 * k);
+                    tc::mma_tf32(dsmall, ahi, bmid, idesc, acc_small);
+                    tc::mma_tf32(dsmall, amid, bhi, idesc, 1u);
+                    tc::mma_tf32(dsmall, ahi, blo, idesc, 1u);
+                    tc::mma_tf32(dsmall, amid, bmid, idesc, 1u);
+                    tc::mma_tf32(dsmall, alo, bhi, idesc, 1u);
+                }
+            }
+            tc::mma_commit(&bars[bi]);
+            if (c % GROUP == GROUP - 1 || c == nchunks - 1) tc::mma_commit(&bars[2 + (g & 1)]);
+        }
+        if (c % GROUP == 0 && g >= 1) return drain(g - 1, false);
+        return true;
+    };
+
+    float ra0[16], rb0[16], ra1[16], rb1[16];
+    load(0, ra0, rb0);
+    if (nchunks > 1) load(1, ra1, rb1);
+    bool ok = true;
+    for (int c = 0; c < nchunks && ok; c += 2) {
+        ok = chunk(c, ra0, rb0);
+        if (ok && c + 1 < nchunks) ok = chunk(c + 1, ra1, rb1);
+    }
+    if (ok) ok = drain((nchunks - 1) / GROUP, true);
+
+    if (ok) {
+        const int row = (warp & 3) * 32 + lane;
+        float* ptile = P + ((size_t)(b * gp.S + sp) * gp.tiles + tile) * TILE * TILE;
+        float* out = ptile + (size_t)row * TILE + (warp >> 2) * 64;
+#pragma unroll
+        for (int i = 0; i < 64; i += 4)
+            *reinterpret_cast<float4*>(out + i) =
+                make_float4(__double2float_rn(acc[i]), __double2float_rn(acc[i + 1]), __double2float_rn(acc[i + 2]),
+                            __double2float_rn(acc[i + 3]));
+        if (diag) {
+            // fixed-order sum of the 8 partial sums of squares of each column: lanes l, l^8, l^16, l^24 of a warp,
+            // then the warp pair (w, w + 4); overwrite the diagonal of the partial tile
+            double* dsum = reinterpret_cast<double*>(buf0);   // operand buffers are free: every MMA has completed
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                double v = dsq[j];
+                v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
+                v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
+                if (lane < 8) dsum[(warp >> 2) * TILE + mrow[j]] = v;
+            }
+            __syncthreads();
+            if (threadIdx.x < TILE) {
+                const int m = threadIdx.x;
+                ptile[(size_t)m * TILE + m] = __double2float_rn(__dadd_rn(dsum[m], dsum[TILE + m]));
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        atomicOr(status, ERR_TIMEOUT);
+        // a wait ran out: give the MMAs already issued a bounded chance to finish before TMEM is released
+        const int last = nchunks - 1;
+        tc::mbar_wait(&bars[2 + ((last / GROUP) & 1)], (uint32_t)(((last / GROUP) >> 1) & 1));
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
+}
+
+template <int PARTS>
+static cudaError_t launch_parts(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
+                                float* P, int* status, cudaStream_t st) {
+    constexpr int smem = smem_bytes<PARTS>();
+    cudaError_t e = cudaFuncSetAttribute(k_gram_tc<PARTS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    k_gram_tc<PARTS><<<dim3(gp.tiles, gp.S, B), NT, smem, st>>>(p, src, K, n, ld, gp, sc, P, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
+                           int accurate, float* P, int* status, cudaStream_t st) {
+    return accurate ? launch_parts<3>(p, src, K, n, ld, B, gp, sc, P, status, st)
+                    : launch_parts<2>(p, src, K, n, ld, B, gp, sc, P, status, st);
+}
+
+}  // namespace spq

@@ -22,14 +22,13 @@ struct ScaleArg {
     const float* s;           // [B] or null
 };
 
-// Split-K plan of the compensated Gram (candidates/tri.py:365-370 at 148 SMs, tiles of 64, chunks of 32 rows).
+// Split-K plan of the Gram: 128 x 128 tiles of the upper triangle, splits of a fixed number of rows.
 struct GramPlan {
-    int nt;      // tiles per side, n / 64 rounded up
+    int nt;      // tiles per side, n / 128 rounded up
     int tiles;   // upper tiles nt (nt + 1) / 2
     int S;       // splits
-    int KS;      // rows per split (a multiple of 32)
+    int KS;      // rows per split
 };
-GramPlan gram_plan(int K, int n);
 
 cudaError_t launch_setup_strided(MatPtr* tab, const float* X, long long sX, float* Q, long long sQ, int B,
                                  uint32_t* maxbits, int* status, cudaStream_t st);
@@ -40,9 +39,14 @@ cudaError_t launch_setup_host(MatPtr* tab, const float* const* hX, float* const*
                               int* status, cudaStream_t st);
 cudaError_t launch_absmax(PtrArg p, int K, int r, long long ldx, int B, uint32_t* maxbits, cudaStream_t st);
 
-// partial Grams P[b][split][tile][64][64] of the source matrix (ld) scaled as `sc`
-cudaError_t launch_gram_partial(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
-                                float* P, cudaStream_t st);
+// tensor-core Gram: 128 x 128 tiles, splits of GRAM_TC_SPLIT rows (a multiple of 128); partials
+// P[b][split][tile][128][128]; a bounded wait that runs out ORs 0x10 into *status
+constexpr int GRAM_TC_SPLIT = 512;
+GramPlan gram_tc_plan(int K, int n);
+// accurate: exact three-way split and six products (the reference's compensated Grams); else two-way, three products
+cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
+                           int accurate, float* P, int* status, cudaStream_t st);
+
 // G[b] (n x n, both triangles) = fp64 sum over splits; with make_D, D = 0.5 (I - G) instead
 cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G,
                                cudaStream_t st);

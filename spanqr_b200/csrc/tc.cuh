@@ -1,0 +1,166 @@
+// sm_100a tensor-core building blocks: TMEM allocation, tcgen05.mma (kind::tf32), commits to mbarriers, TMEM
+// loads, proxy fences, split-TF32 conversion and the shared-memory layout the MMA reads (K-major, 128-byte swizzle).
+//
+// Operand tiles: R rows (M or N) x 32 fp32 (one 128-byte row per M/N index), stored as 8-row atoms of 1024 bytes;
+// the 16-byte chunk c (k = 4c .. 4c+3) of row m sits at chunk position c ^ (m % 8).  Tile bases are 1024-aligned.
+// One MMA consumes K = 8 (32 bytes); k-step s starts 32 * s bytes into the tile.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spq {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ---- mbarriers ----
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase with this parity to complete, for at most `limit_ns`; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+
+// ---- proxy and tcgen05 ordering fences ----
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- tensor memory (executed by one full warp) ----
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- MMA: D[tmem] (+)= A[smem] * B[smem]^T, fp32 accumulate, tf32 inputs, issued by one thread ----
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        :
+        : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// arrive (once) on `bar` when every MMA this thread issued before has completed
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// instruction descriptor: D fp32, A and B tf32, both K-major, M x N
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart
+__device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)64u << 32) | ((uint64_t)1u << 46) |
+           ((uint64_t)2u << 61);
+}
+
+// ---- TMEM -> registers: this warp's 32 lanes, 32 consecutive 32-bit columns ----
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- split TF32: x = hi + lo (+ a remainder below 2^-22 |x|), both rounded to tf32 (low 13 bits zero) ----
+__device__ __forceinline__ float to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    hi = to_tf32(x);
+    lo = to_tf32(__fsub_rn(x, hi));
+}
+
+// exact three-way split x = hi + mid + lo (11 + 11 + the remaining 2 bits), each a tf32 value
+__device__ __forceinline__ void split3_tf32(float x, float& hi, float& mid, float& lo) {
+    hi = to_tf32(x);
+    const float r1 = __fsub_rn(x, hi);
+    mid = to_tf32(r1);
+    lo = to_tf32(__fsub_rn(r1, mid));
+}
+
+// byte offset of the 16-byte chunk (row m, k-quad q) inside a K-major 128B-swizzled tile
+__device__ __forceinline__ uint32_t swz_off(int m, int q) {
+    return (uint32_t)((m >> 3) * 1024 + (m & 7) * 128 + ((q ^ (m & 7)) << 4));
+}
+
+// store 4 consecutive k of row m (k-quad q) as hi and lo tf32 into two tiles
+__device__ __forceinline__ void store_split4(char* hi_tile, char* lo_tile, int m, int q, float4 v) {
+    float4 h, l;
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+    const uint32_t o = swz_off(m, q);
+    *reinterpret_cast<float4*>(hi_tile + o) = h;
+    *reinterpret_cast<float4*>(lo_tile + o) = l;
+}
+
+// store 4 consecutive k of row m (k-quad q) as hi, mid and lo tf32 into three tiles
+__device__ __forceinline__ void store_split4x3(char* hi_tile, char* mid_tile, char* lo_tile, int m, int q, float4 v) {
+    float4 h, md, l;
+    split3_tf32(v.x, h.x, md.x, l.x);
+    split3_tf32(v.y, h.y, md.y, l.y);
+    split3_tf32(v.z, h.z, md.z, l.z);
+    split3_tf32(v.w, h.w, md.w, l.w);
+    const uint32_t o = swz_off(m, q);
+    *reinterpret_cast<float4*>(hi_tile + o) = h;
+    *reinterpret_cast<float4*>(mid_tile + o) = md;
+    *reinterpret_cast<float4*>(lo_tile + o) = l;
+}
+
+}  // namespace tc
+}  // namespace spq

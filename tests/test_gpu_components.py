@@ -1,8 +1,10 @@
 """Each CUDA kernel family against the oracle, through the C ABI.
 
-The clamped Cholesky (k_chol) evaluates exactly the oracle's operation sequence (chol.cu's), so its L and Li must
-equal the oracle's bit for bit.  The split Gram and the row-block solve are held to the same bar while they run the
-oracle's order; the golden Gram is the reference's own gram_f output."""
+The clamped Cholesky (k_chol) and the row-block solve (k_trsm) evaluate exactly the oracle's operation sequence
+(chol.cu's and tri.py's), so their outputs must equal the oracle's bit for bit.  The tensor-core Gram (k_gram_tc,
+split-TF32) rounds differently from any CPU order: it is held to an elementwise bound of GRAM_ULPS units of fp32
+rounding of sum_k |y_ki| |y_kj| against the exact (fp64) Gram (on its fixture the reference's own compensated gram_f
+is 19.5 units off)."""
 from pathlib import Path
 
 import numpy as np
@@ -49,19 +51,44 @@ def test_chol_bitwise_golden_and_clamped():
     assert gu.bits_equal(L, Lo) and gu.bits_equal(Li, Lio)
 
 
+GRAM_ULPS = 8
+U32 = 2.0 ** -24
+
+
+def gram_bound_ok(G, Y, s=None):
+    Y64 = Y.astype(np.float64) * (s if s is not None else 1.0)
+    exact = Y64.T @ Y64
+    scale = np.abs(Y64).T @ np.abs(Y64)
+    err = np.abs(G.astype(np.float64) - exact)
+    return float((err / np.maximum(scale, 1e-300)).max() / U32)
+
+
 @pytest.mark.parametrize("K,n,scaled", [(100, 64, False), (777, 96, True), (3584, 256, True), (2048, 512, False),
-                                        (17408, 256, False)])
-def test_gram_bitwise(K, n, scaled):
+                                        (17408, 256, False), (513, 160, True)])
+def test_gram_within_bound(K, n, scaled):
     rng = np.random.default_rng(K + n)
     Y = (rng.standard_normal((K, n)) * 3.0).astype(np.float32)
     s = 0.25 if scaled else None
-    assert gu.bits_equal(gu.gram(Y, s), oracle.gram_kahan(Y, s=s))
+    G = gu.gram(Y, s)
+    assert np.array_equal(G, G.T)
+    ulps = gram_bound_ok(G, Y, s)
+    assert ulps <= GRAM_ULPS, ulps
 
 
-def test_gram_equals_reference_gram_f():
+def test_gram_close_to_reference_gram_f():
     """the golden G0 is the reference's own tri.gram_f(X, s) (run by Triton's interpreter)"""
     g = np.load(GOLD / "golden.npz")
-    assert gu.bits_equal(gu.gram(g["comp/X"], float(g["comp/s"][0])), g["comp/G0"])
+    X, s = g["comp/X"], float(g["comp/s"][0])
+    G = gu.gram(X, s)
+    mine, ref = gram_bound_ok(G, X, s), gram_bound_ok(g["comp/G0"], X, s)
+    assert mine <= max(GRAM_ULPS, ref), (mine, ref)
+
+
+def test_gram_ill_scaled_columns():
+    """columns spanning 1e-12 .. 1: the bound holds column pair by column pair"""
+    rng = np.random.default_rng(7)
+    Y = (rng.standard_normal((1024, 128)) * np.logspace(0, -12, 128)).astype(np.float32)
+    assert gram_bound_ok(gu.gram(Y), Y) <= GRAM_ULPS
 
 
 @pytest.mark.parametrize("K,n", [(100, 64), (1000, 256), (777, 512)])

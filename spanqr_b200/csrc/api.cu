@@ -145,7 +145,10 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
                                   status, st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, st); }));
-        SPQ_TRY(timed(K_NS, st, [&] { return launch_ns_update(p, K, r, ldq, B, G, st); }));
+        // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel
+        SPQ_TRY(timed(K_NS, st, [&] {
+            return r <= 256 ? launch_ns_tc(p, K, r, ldq, B, G, status, st) : launch_ns_update(p, K, r, ldq, B, G, st);
+        }));
     }
 #undef SPQ_TRY
     return SPANQR_OK;

@@ -1,9 +1,11 @@
 // Gram G = A^T A (A = s Y, Y [K, n] fp32 row-major) on the 5th-generation tensor cores, split-TF32 (3xTF32).
 //
-// One CTA = one 128 x 128 tile (ti <= tj) of the upper triangle of G over one 512-row split of Y.  Per 32-row chunk:
-// the 256 threads load the two 32 x 128 column panels (coalesced 32-byte row segments), split every value into
-// tf32 parts and store them K-major into 128B-swizzled shared tiles (the Gram contracts over the rows of Y, so this
-// is the transpose the MMA wants); one thread then issues, per k-step of 8 rows, tcgen05.mma M128 N128 K8 products:
+// One CTA = one 128 x 128 tile (ti <= tj) of the upper triangle of G over one 512-row split of Y.  Per 32-row chunk
+// the 256 threads load the two 32 x 128 column panels with coalesced 16-byte loads (warp w: rows 4w .. 4w+3, lane l:
+// columns 4l .. 4l+3), split every value into tf32 parts and store them into MN-major shared tiles (128-byte swizzle
+// on a 32-byte base, the MN-major layout tcgen05 takes for tf32) --
+// the Gram contracts over the rows of Y, so Y's own row-major layout is the MN-major operand layout and no transpose
+// is needed; one thread then issues, per k-step of 8 rows, tcgen05.mma M128 N128 K8 products:
 //   plain mode    (x = hi + lo, 22 of 24 bits): hi.hi | hi.lo + lo.hi                                   (3 MMAs)
 //   accurate mode (x = hi + mid + lo exactly):  hi.hi | hi.mid + mid.hi + hi.lo + mid.mid + lo.hi      (6 MMAs)
 // hi.hi goes to one TMEM accumulator and the small products to a second one, so the small terms never round
@@ -92,52 +94,49 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    // this thread's four (row m, k-quad q) slots of a 32 x 128 panel: warps 0-3 take k-quads 0-3, warps 4-7 4-7;
-    // inside a warp 8 consecutive m (one swizzle atom) x 4 k-quads, so the 16-byte stores hit distinct banks
-    const int q = (warp >> 2) * 4 + (lane >> 3);
-    int mrow[4];
+    // this thread's slots of a 32 x 128 panel: rows 4 * warp + i (i = 0..3), columns 4 * lane .. 4 * lane + 3; a
+    // warp's 16-byte stores for one row fill one 128-byte row of each of the 4 MN-atoms: no bank conflict
+    const int colA = ti * TILE + 4 * lane, colB = tj * TILE + 4 * lane;
+    const bool inA = colA < n, inB = !diag && colB < n;   // n is a multiple of 32, so 4 columns are in or out together
+    uint32_t soff[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) mrow[j] = 8 * ((warp & 3) * 4 + j) + (lane & 7);
-    const int colA = ti * TILE, colB = tj * TILE;
+    for (int i = 0; i < 4; ++i) soff[i] = tc::swz_mn_off(4 * warp + i, 4 * lane);
 
-    auto load = [&](int c, float (&ra)[16], float (&rb)[16]) {
-        const int row0 = k0 + c * CHUNK + 4 * q;
+    auto load = [&](int c, float4 (&ra)[4], float4 (&rb)[4]) {
+        const int row0 = k0 + c * CHUNK + 4 * warp;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int row = row0 + i;
-            const bool rin = row < k1;
             const float* yr = Y + (long long)row * ld;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float va = 0.0f, vb = 0.0f;
-                if (rin && colA + mrow[j] < n) va = __ldg(yr + colA + mrow[j]);
-                if (rin && !diag && colB + mrow[j] < n) vb = __ldg(yr + colB + mrow[j]);
-                ra[j * 4 + i] = scaled ? __fmul_rn(va, s) : va;
-                rb[j * 4 + i] = scaled ? __fmul_rn(vb, s) : vb;
+            float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+            if (row < k1) {
+                if (inA) va = __ldg(reinterpret_cast<const float4*>(yr + colA));
+                if (inB) vb = __ldg(reinterpret_cast<const float4*>(yr + colB));
             }
+            if (scaled) {
+                va.x = __fmul_rn(va.x, s); va.y = __fmul_rn(va.y, s); va.z = __fmul_rn(va.z, s); va.w = __fmul_rn(va.w, s);
+                vb.x = __fmul_rn(vb.x, s); vb.y = __fmul_rn(vb.y, s); vb.z = __fmul_rn(vb.z, s); vb.w = __fmul_rn(vb.w, s);
+            }
+            ra[i] = va;
+            rb[i] = vb;
         }
     };
-    double dsq[4] = {0.0, 0.0, 0.0, 0.0};   // diagonal tiles: sum of squares of column colA + mrow[j]
-    auto stage = [&](int bi, const float (&ra)[16], const float (&rb)[16]) {
+    double dsq[4] = {0.0, 0.0, 0.0, 0.0};   // diagonal tiles: sums of squares of columns colA .. colA + 3
+    auto stage = [&](int bi, const float4 (&ra)[4], const float4 (&rb)[4]) {
         char* base = buf0 + bi * BUF;
-        if (diag) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) dsq[j] = __fma_rn((double)ra[j * 4 + i], (double)ra[j * 4 + i], dsq[j]);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float4 v = make_float4(ra[j * 4], ra[j * 4 + 1], ra[j * 4 + 2], ra[j * 4 + 3]);
-            if constexpr (PARTS == 2) tc::store_split4(base, base + OPND, mrow[j], q, v);
-            else tc::store_split4x3(base, base + OPND, base + 2 * OPND, mrow[j], q, v);
-        }
-        if (!diag) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 v = make_float4(rb[j * 4], rb[j * 4 + 1], rb[j * 4 + 2], rb[j * 4 + 3]);
-                if constexpr (PARTS == 2) tc::store_split4(base + BOFF, base + BOFF + OPND, mrow[j], q, v);
-                else tc::store_split4x3(base + BOFF, base + BOFF + OPND, base + BOFF + 2 * OPND, mrow[j], q, v);
+        for (int i = 0; i < 4; ++i) {
+            if (diag) {
+                dsq[0] = __fma_rn((double)ra[i].x, (double)ra[i].x, dsq[0]);
+                dsq[1] = __fma_rn((double)ra[i].y, (double)ra[i].y, dsq[1]);
+                dsq[2] = __fma_rn((double)ra[i].z, (double)ra[i].z, dsq[2]);
+                dsq[3] = __fma_rn((double)ra[i].w, (double)ra[i].w, dsq[3]);
+            }
+            if constexpr (PARTS == 2) tc::store2_at(base, base + OPND, soff[i], ra[i]);
+            else tc::store3_at(base, base + OPND, base + 2 * OPND, soff[i], ra[i]);
+            if (!diag) {
+                if constexpr (PARTS == 2) tc::store2_at(base + BOFF, base + BOFF + OPND, soff[i], rb[i]);
+                else tc::store3_at(base + BOFF, base + BOFF + OPND, base + BOFF + 2 * OPND, soff[i], rb[i]);
             }
         }
     };
@@ -145,7 +144,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
     double acc[64];   // rows (warp & 3) * 32 + lane, columns (warp >> 2) * 64 .. + 64
 #pragma unroll
     for (int i = 0; i < 64; ++i) acc[i] = 0.0;
-    const uint32_t idesc = tc::idesc_tf32(TILE, TILE);
+    const uint32_t idesc = tc::idesc_tf32_mn(TILE, TILE);
     const uint32_t tq = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * 64);
     const uint32_t tsmall = tmem + 2 * TILE;
 
@@ -172,7 +171,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
         return true;
     };
 
-    auto chunk = [&](int c, float (&ra)[16], float (&rb)[16]) -> bool {
+    auto chunk = [&](int c, float4 (&ra)[4], float4 (&rb)[4]) -> bool {
         const int bi = c & 1;
         bool ok = true;
         if (c >= 2) ok = tc::mbar_wait(&bars[bi], (uint32_t)(((c - 2) >> 1) & 1));
@@ -192,14 +191,18 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
             for (int k = 0; k < CHUNK / 8; ++k) {
                 const uint32_t acc_in = (c % GROUP != 0 || k > 0) ? 1u : 0u;          // large: per group
                 const uint32_t acc_small = (c != 0 || k > 0) ? 1u : 0u;              // small: whole split
-                const uint64_t ahi = tc::sdesc_k128(abase + 32 * k), alo = tc::sdesc_k128(abase + (PARTS - 1) * OPND + 32 * k);
-                const uint64_t bhi = tc::sdesc_k128(bbase + 32 * k), blo = tc::sdesc_k128(bbase + (PARTS - 1) * OPND + 32 * k);
+                // k-step k = rows 8k .. 8k+7 of the chunk = k-atoms 2k, 2k+1 (2048 bytes apart); MN-atoms 512 apart
+                const uint64_t ahi = tc::sdesc_mn128b32(abase + 4096 * k, 512, 2048);
+                const uint64_t alo = tc::sdesc_mn128b32(abase + (PARTS - 1) * OPND + 4096 * k, 512, 2048);
+                const uint64_t bhi = tc::sdesc_mn128b32(bbase + 4096 * k, 512, 2048);
+                const uint64_t blo = tc::sdesc_mn128b32(bbase + (PARTS - 1) * OPND + 4096 * k, 512, 2048);
                 tc::mma_tf32(dbig, ahi, bhi, idesc, acc_in);
                 if constexpr (PARTS == 2) {
                     tc::mma_tf32(dsmall, ahi, blo, idesc, acc_small);
                     tc::mma_tf32(dsmall, alo, bhi, idesc, 1u);
                 } else {
-                    const uint64_t amid = tc::sdesc_k128(abase + OPND + 32 * k), bmid = tc::sdesc_k128(bbase + OPND + 32 * k);
+                    const uint64_t amid = tc::sdesc_mn128b32(abase + OPND + 4096 * k, 512, 2048);
+                    const uint64_t bmid = tc::sdesc_mn128b32(bbase + OPND + 4096 * k, 512, 2048);
                     tc::mma_tf32(dsmall, ahi, bmid, idesc, acc_small);
                     tc::mma_tf32(dsmall, amid, bhi, idesc, 1u);
                     tc::mma_tf32(dsmall, ahi, blo, idesc, 1u);
@@ -214,7 +217,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
         return true;
     };
 
-    float ra0[16], rb0[16], ra1[16], rb1[16];
+    float4 ra0[4], rb0[4], ra1[4], rb1[4];
     load(0, ra0, rb0);
     if (nchunks > 1) load(1, ra1, rb1);
     bool ok = true;
@@ -234,20 +237,17 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
                 make_float4(__double2float_rn(acc[i]), __double2float_rn(acc[i + 1]), __double2float_rn(acc[i + 2]),
                             __double2float_rn(acc[i + 3]));
         if (diag) {
-            // fixed-order sum of the 8 partial sums of squares of each column: lanes l, l^8, l^16, l^24 of a warp,
-            // then the warp pair (w, w + 4); overwrite the diagonal of the partial tile
+            // fixed-order sum of the 8 warps' partial sums of squares of each column (warp order 0..7); overwrite the
+            // diagonal of the partial tile
             double* dsum = reinterpret_cast<double*>(buf0);   // operand buffers are free: every MMA has completed
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                double v = dsq[j];
-                v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 8));
-                v = __dadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 16));
-                if (lane < 8) dsum[(warp >> 2) * TILE + mrow[j]] = v;
-            }
+            for (int j = 0; j < 4; ++j) dsum[warp * TILE + 4 * lane + j] = dsq[j];
             __syncthreads();
             if (threadIdx.x < TILE) {
                 const int m = threadIdx.x;
-                ptile[(size_t)m * TILE + m] = __double2float_rn(__dadd_rn(dsum[m], dsum[TILE + m]));
+                double t = dsum[m];
+                for (int w = 1; w < NT / 32; ++w) t = __dadd_rn(t, dsum[w * TILE + m]);
+                ptile[(size_t)m * TILE + m] = __double2float_rn(t);
             }
         }
     } else if (threadIdx.x == 0) {

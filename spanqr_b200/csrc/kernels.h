@@ -62,6 +62,10 @@ cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const doubl
 cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
                         ScaleArg sc, float eps, const float* L, const float* Li, cudaStream_t st);
 
+// Q <- Q + Q D per matrix on the tensor cores, in place (D symmetric, n x n per matrix), n <= 256; a bounded wait that
+// runs out ORs 0x20 into *status
+cudaError_t launch_ns_tc(PtrArg p, int K, int n, long long ldq, int B, const float* D, int* status, cudaStream_t st);
+
 // Q <- Q + Q D per matrix, in place (D symmetric, n x n per matrix)
 cudaError_t launch_ns_update(PtrArg p, int K, int n, long long ldq, int B, const float* D, cudaStream_t st);
 

@@ -94,6 +94,27 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
            ((uint64_t)2u << 61);
 }
 
+// shared-memory matrix descriptor: MN-major tf32, 128-byte swizzle on a 32-byte base (layout type 1, the only
+// MN-major layout tcgen05 accepts for 32-bit operands).  Atoms of 4 k-rows x 32 MN-elements (512 bytes) in which the
+// 32-byte granule g of k-row r sits at granule position g ^ r; atoms along MN are `mn_stride` bytes apart (leading
+// byte offset), along K `k_stride` bytes apart (stride byte offset).
+__device__ __forceinline__ uint64_t sdesc_mn128b32(uint32_t saddr, uint32_t mn_stride, uint32_t k_stride) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((mn_stride >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((k_stride >> 4) & 0x3FFFu) << 32) | ((uint64_t)1u << 46) | ((uint64_t)1u << 61);
+}
+
+// instruction descriptor: D fp32, A and B tf32, both MN-major, M x N
+__host__ __device__ constexpr uint32_t idesc_tf32_mn(int M, int N) {
+    return idesc_tf32(M, N) | (1u << 15) | (1u << 16);
+}
+
+// byte offset of (k, mn .. mn+3) (mn a multiple of 4) in an MN-major tile of 128 MN x 32 k in the 32-byte-base
+// layout: MN-atoms (32 elements) 512 bytes apart, k-atoms (4 rows) 2048 bytes apart
+__device__ __forceinline__ uint32_t swz_mn_off(int k, int mn) {
+    const int kr = k & 3, g = (mn >> 3) & 3;
+    return (uint32_t)((k >> 2) * 2048 + (mn >> 5) * 512 + kr * 128 + ((g ^ kr) << 5) + ((mn & 7) << 2));
+}
+
 // ---- TMEM -> registers: this warp's 32 lanes, 32 consecutive 32-bit columns ----
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
@@ -113,10 +134,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---- split TF32: x = hi + lo (+ a remainder below 2^-22 |x|), both rounded to tf32 (low 13 bits zero) ----
+// Round to nearest, ties away from zero, on the bit pattern: add half a tf32 ulp to the magnitude bits and clear
+// the 13 low bits (two integer ops on the ALU, where the conversion instruction would occupy the slower XU pipe).
+// Finite inputs only (an infinity would turn into a NaN).
 __device__ __forceinline__ float to_tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
@@ -146,6 +168,28 @@ __device__ __forceinline__ void store_split4(char* hi_tile, char* lo_tile, int m
     split_tf32(v.w, h.w, l.w);
     const uint32_t o = swz_off(m, q);
     *reinterpret_cast<float4*>(hi_tile + o) = h;
+    *reinterpret_cast<float4*>(lo_tile + o) = l;
+}
+
+// store the split parts of v at byte offset o of two (hi, lo) or three (hi, mid, lo) tiles
+__device__ __forceinline__ void store2_at(char* hi_tile, char* lo_tile, uint32_t o, float4 v) {
+    float4 h, l;
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+    *reinterpret_cast<float4*>(hi_tile + o) = h;
+    *reinterpret_cast<float4*>(lo_tile + o) = l;
+}
+
+__device__ __forceinline__ void store3_at(char* hi_tile, char* mid_tile, char* lo_tile, uint32_t o, float4 v) {
+    float4 h, md, l;
+    split3_tf32(v.x, h.x, md.x, l.x);
+    split3_tf32(v.y, h.y, md.y, l.y);
+    split3_tf32(v.z, h.z, md.z, l.z);
+    split3_tf32(v.w, h.w, md.w, l.w);
+    *reinterpret_cast<float4*>(hi_tile + o) = h;
+    *reinterpret_cast<float4*>(mid_tile + o) = md;
     *reinterpret_cast<float4*>(lo_tile + o) = l;
 }
 

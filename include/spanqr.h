@@ -119,7 +119,8 @@ int spanqr_chol_f32(const float* G, int n, const float* d_tau, float* L, float* 
  *   Z [K, n] (leading dimension n) or NULL, d_s device pointer to s or NULL for s = 1.  Y may equal X (in place).
  */
 int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* d_s, float eps, const float* L,
-                    const float* Li, int K, int n, float* Y, long long ldy, spanqr_stream_t stream);
+                    const float* Li, int K, int n, float* Y, long long ldy, void* ws, size_t ws_bytes,
+                    spanqr_stream_t stream);
 
 /*
  * Kernel timing (no reference counterpart; the reference stamps %globaltimer under CHOL_DEBUG, chol.cu:17-23).

@@ -20,7 +20,7 @@ SIGNATURES = {
     "spanqr_orth_ptrs_f32": (_I, [_P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
     "spanqr_gram_f32": (_I, [_P, _LL, _I, _I, _P, _P, _P, _SZ, _P]),
     "spanqr_chol_f32": (_I, [_P, _I, _P, _P, _P, _P, _SZ, _P]),
-    "spanqr_trsm_f32": (_I, [_P, _LL, _P, _P, _F, _P, _P, _I, _I, _P, _LL, _P]),
+    "spanqr_trsm_f32": (_I, [_P, _LL, _P, _P, _F, _P, _P, _I, _I, _P, _LL, _P, _SZ, _P]),
     "spanqr_read_status": (_I, [_P, _P, ctypes.POINTER(_I)]),
     "spanqr_orth_noalloc_f32": (_I, [_P, _LL, _P, _LL, _I, _I, _P, _P]),
     "spanqr_timing_enable": (_I, [_I]),

@@ -135,8 +135,10 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
             return launch_chol(G, Lm, Li, r, B, rowsq, nullptr, scal + (size_t)pass * B, 0, st);
         }));
         SPQ_TRY(timed(K_TRSM, st, [&] {
-            return launch_trsm(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
-                               first ? EPS : 0.0f, Lm, Li, st);
+            return r <= 256 ? launch_trsm_tc(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
+                                             first ? EPS : 0.0f, Lm, Li, status, st)
+                            : launch_trsm(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
+                                          first ? EPS : 0.0f, Lm, Li, st);
         }));
     }
     for (int it = 0; it < NS_STEPS; ++it) {
@@ -315,14 +317,21 @@ int spanqr_chol_f32(const float* G, int n, const float* d_tau, float* L, float* 
 }
 
 int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* d_s, float eps, const float* L,
-                    const float* Li, int K, int n, float* Y, long long ldy, spanqr_stream_t stream) {
+                    const float* Li, int K, int n, float* Y, long long ldy, void* ws, size_t ws_bytes,
+                    spanqr_stream_t stream) {
     int rc = check_shape(K, n, 1);
     if (rc) return rc;
     if (!X || !Y || !L || !Li || !a16(X) || !a16(Y) || (Z && !a16(Z))) return SPANQR_ERR_ARG;
     if (ldx < n || ldy < n || ldx % 4 || ldy % 4) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, n, 1))) return rc;
+    const Layout l = layout(K, n, 1);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     PtrArg p{nullptr, MatPtr{X, Y}};
-    cudaError_t e = launch_trsm(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li, st);
+    cudaError_t e = cudaMemsetAsync(at<int>(ws, l.status), 0, sizeof(int), st);
+    if (e == cudaSuccess)
+        e = n <= 256 ? launch_trsm_tc(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li,
+                                      at<int>(ws, l.status), st)
+                     : launch_trsm(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 

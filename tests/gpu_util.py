@@ -54,9 +54,11 @@ def trsm(X, L, Li, s=None, Z=None, eps=0.0, inplace=False):
     Y = X if inplace else torch.empty_like(X)
     Zt = cu(Z) if Z is not None else None
     sp = cu(np.array([s], np.float32)) if s is not None else None
+    w = ws(K, n)
     _lib.check(_lib.lib().spanqr_trsm_f32(X.data_ptr(), n, Zt.data_ptr() if Zt is not None else None,
                                           sp.data_ptr() if sp is not None else None, ctypes.c_float(eps),
-                                          L.data_ptr(), Li.data_ptr(), K, n, Y.data_ptr(), n, stream()), "trsm")
+                                          L.data_ptr(), Li.data_ptr(), K, n, Y.data_ptr(), n, w.data_ptr(), w.numel(),
+                                          stream()), "trsm")
     return Y.cpu().numpy()
 
 

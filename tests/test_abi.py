@@ -57,7 +57,7 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_orth_f32(al, 64, al, 64, 256, 64, al, al + 16, ws_need, None) == WS     # workspace misaligned
     assert L.spanqr_orth_strided_f32(al, 64, 64 * 256, al, 64, 10, 256, 64, 2, al, al, 10 ** 9, None) == ARG  # overlap
     assert L.spanqr_chol_f32(al, 100, al, al, al, al, 10 ** 9, None) == SHAPE
-    assert L.spanqr_trsm_f32(al, 64, None, None, 0.0, al, al, 256, 64, al, 60, None) == ARG
+    assert L.spanqr_trsm_f32(al, 64, None, None, 0.0, al, al, 256, 64, al, 60, al, 10 ** 9, None) == ARG
     assert L.spanqr_gram_f32(al, 64, 32, 64, None, al, al, 10 ** 9, None) == SHAPE           # K < n
     st = ctypes.c_int(7)
     assert L.spanqr_read_status(None, None, ctypes.byref(st)) == ARG

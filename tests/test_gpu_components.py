@@ -1,7 +1,8 @@
 """Each CUDA kernel family against the oracle, through the C ABI.
 
-The clamped Cholesky (k_chol) and the row-block solve (k_trsm) evaluate exactly the oracle's operation sequence
-(chol.cu's and tri.py's), so their outputs must equal the oracle's bit for bit.  The tensor-core Gram (k_gram_tc,
+The clamped Cholesky (k_chol) evaluates exactly the oracle's operation sequence (chol.cu's), so its output must equal
+the oracle's bit for bit; so must the row-block solve (k_trsm, rows wider than 256).  The tensor-core solve
+(k_trsm_tc) is held to the forward-error bound of a backward-stable solve.  The tensor-core Gram (k_gram_tc,
 split-TF32) rounds differently from any CPU order: it is held to an elementwise bound of GRAM_ULPS units of fp32
 rounding of sum_k |y_ki| |y_kj| against the exact (fp64) Gram (on its fixture the reference's own compensated gram_f
 is 19.5 units off)."""
@@ -91,14 +92,29 @@ def test_gram_ill_scaled_columns():
     assert gram_bound_ok(gu.gram(Y), Y) <= GRAM_ULPS
 
 
-@pytest.mark.parametrize("K,n", [(100, 64), (1000, 256), (777, 512)])
-def test_trsm_bitwise(K, n):
+def trsm_err(Y, X, L, s=1.0, Z=None, eps=0.0):
+    """max |Y - Y_exact| / (max |Y_exact| kappa(L) u32) for Y_exact = (s X + eps Z) L^-T in fp64"""
+    A = X.astype(np.float64) * s + (eps * Z.astype(np.float64) if Z is not None else 0.0)
+    L64 = L.astype(np.float64)
+    ex = np.linalg.solve(L64, A.T).T
+    kappa = np.linalg.cond(L64)
+    return float(np.abs(Y.astype(np.float64) - ex).max() / (np.abs(ex).max() * kappa * U32))
+
+
+@pytest.mark.parametrize("K,n", [(100, 64), (1000, 256), (777, 160), (300, 128), (777, 512)])
+def test_trsm_forward_error(K, n):
+    """the solve's forward error stays within a few units of kappa(L) u32 of the exact solution, like the oracle's;
+    wider than 256 columns the row-block kernel runs, which reproduces the oracle bit for bit"""
     rng = np.random.default_rng(K * n)
     X = rng.standard_normal((K, n)).astype(np.float32)
     G, tau = spd(n, 2 * n, K)
     L, Li = oracle.chol32(G, tau)
     Z = oracle.dust(K, n)
     Y = gu.trsm(X, L, Li, s=0.5, Z=Z, eps=5e-7)
-    assert gu.bits_equal(Y, oracle.trsm(X, L, Li, s=0.5, Z=Z, eps=5e-7))
+    Yo = oracle.trsm(X, L, Li, s=0.5, Z=Z, eps=5e-7)
+    e_gpu, e_or = trsm_err(Y, X, L, 0.5, Z, 5e-7), trsm_err(Yo, X, L, 0.5, Z, 5e-7)
+    assert e_gpu <= max(4.0, 2 * e_or), (e_gpu, e_or)
     Y2 = gu.trsm(X, L, Li, inplace=True)
-    assert gu.bits_equal(Y2, oracle.trsm(X, L, Li))
+    assert trsm_err(Y2, X, L) <= max(4.0, 2 * trsm_err(oracle.trsm(X, L, Li), X, L))
+    if n > 256:
+        assert gu.bits_equal(Y, Yo)

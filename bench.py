@@ -176,7 +176,7 @@ def alg_bytes_per_matrix(kind, K, r):
     kr4 = 4.0 * K * r
     return {"k_absmax": kr4, "k_gram_tc": kr4, "k_trsm": (3 + 2 + 2) * kr4 / 3.0,
             "k_ns_update": 2 * kr4, "k_gram_reduce": 4.0 * r * r, "k_rowsq": 4.0 * r * r,
-            "k_chol": 3 * 4.0 * r * r, "k_setup": 16.0}.get(kind, 0.0)
+            "k_chol": 3 * 4.0 * r * r, "k_trsm_w": 4.0 * r * r, "k_setup": 16.0}.get(kind, 0.0)
 
 
 def dist_max(x, device):

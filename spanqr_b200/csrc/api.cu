@@ -28,9 +28,9 @@ int cuda_fail(cudaError_t e) {
 }
 
 // ---- optional per-kernel timing (spanqr_timing_*) ----
-enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM, K_NS, K_COUNT };
+enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_COUNT };
 const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce", "k_rowsq",
-                                         "k_chol", "k_trsm", "k_ns_update"};
+                                         "k_chol", "k_trsm_w", "k_trsm", "k_ns_update"};
 struct TimedLaunch {
     int kind;
     cudaEvent_t a, b;
@@ -66,7 +66,7 @@ cudaError_t timed(int kind, cudaStream_t st, F&& launch) {
 size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, P, total;
+    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, W, P, total;
 };
 
 Layout layout(int K, int r, int B) {
@@ -81,6 +81,7 @@ Layout layout(int K, int r, int B) {
     l.G = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.L = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
+    l.W = o;       o += (r <= 256) ? al256(trsm_w_bytes(r) * (size_t)B) : 0;
     l.P = o;       o += al256(sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE);
     l.total = o;
     return l;
@@ -115,6 +116,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
     float* G = at<float>(ws, l.G);
     float* Lm = at<float>(ws, l.L);
     float* Li = at<float>(ws, l.Li);
+    char* W = at<char>(ws, l.W);
     float* P = at<float>(ws, l.P);
     cudaError_t e;
 #define SPQ_TRY(call)                          \
@@ -134,9 +136,10 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         SPQ_TRY(timed(K_CHOL, st, [&] {
             return launch_chol(G, Lm, Li, r, B, rowsq, nullptr, scal + (size_t)pass * B, 0, st);
         }));
+        if (r <= 256) SPQ_TRY(timed(K_TRSM_W, st, [&] { return launch_trsm_w(Lm, Li, r, B, W, st); }));
         SPQ_TRY(timed(K_TRSM, st, [&] {
             return r <= 256 ? launch_trsm_tc(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
-                                             first ? EPS : 0.0f, Lm, Li, status, st)
+                                             first ? EPS : 0.0f, W, status, st)
                             : launch_trsm(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
                                           first ? EPS : 0.0f, Lm, Li, st);
         }));
@@ -328,9 +331,10 @@ int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     PtrArg p{nullptr, MatPtr{X, Y}};
     cudaError_t e = cudaMemsetAsync(at<int>(ws, l.status), 0, sizeof(int), st);
+    if (e == cudaSuccess && n <= 256) e = launch_trsm_w(L, Li, n, 1, at<char>(ws, l.W), st);
     if (e == cudaSuccess)
-        e = n <= 256 ? launch_trsm_tc(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li,
-                                      at<int>(ws, l.status), st)
+        e = n <= 256 ? launch_trsm_tc(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f,
+                                      at<char>(ws, l.W), at<int>(ws, l.status), st)
                      : launch_trsm(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }

@@ -58,9 +58,12 @@ cudaError_t launch_rowsq(const float* G, int n, int B, double* rowsq, cudaStream
 cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, const float* tau_ptr,
                         PassScal* scal, int zero_upper, cudaStream_t st);
 
-// the same on the tensor cores, n <= 256; a bounded wait that runs out ORs 0x40 into *status
+// the solve's coefficient image W (W_jj = Li_j, W_jk = -Li_j L_jk, split tf32 tiles), trsm_w_bytes(n) per matrix
+size_t trsm_w_bytes(int n);
+cudaError_t launch_trsm_w(const float* L, const float* Li, int n, int B, char* W, cudaStream_t st);
+// the same solve on the tensor cores from the image W, n <= 256; a bounded wait that runs out ORs 0x40 into *status
 cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
-                           ScaleArg sc, float eps, const float* L, const float* Li, int* status, cudaStream_t st);
+                           ScaleArg sc, float eps, const char* W, int* status, cudaStream_t st);
 
 // Y = (s X + eps Z) L^-T per matrix: input from `src`, output to Q (in place when src == SRC_Q)
 cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,

@@ -208,3 +208,15 @@ __device__ __forceinline__ void store_split4x3(char* hi_tile, char* mid_tile, ch
 
 }  // namespace tc
 }  // namespace spq
+
+namespace spq {
+namespace tc {
+// ---- 16-byte asynchronous global -> shared copies (no registers; completion per thread via groups) ----
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+}  // namespace tc
+}  // namespace spq

@@ -262,6 +262,156 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
     if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// Plain mode (the reference's SGEMM Grams: passes 2 and 3 and the first polish step): two CTAs per SM instead of one,
+// so each CTA's load latency and barriers are hidden by the other's work.  Per CTA one operand buffer (hi, lo of both
+// panels: 64 KB), the whole 512-row split accumulated in TMEM (hi.hi and hi.lo + lo.hi in separate 128-column
+// accumulators, 256 columns), no fp64 drains; the exact fp64 diagonal as in the accurate mode.  Same tile/split plan
+// and partial layout as k_gram_tc.
+constexpr int PLAIN_NT = 256;
+constexpr int PLAIN_BUF = 4 * OPND;
+constexpr int PLAIN_SMEM = PLAIN_BUF + 1024 + 1024;
+
+__global__ void __launch_bounds__(PLAIN_NT, 2) k_gram_tc_plain(PtrArg p, Src src, int K, int n, long long ld, GramPlan gp,
+                                                                ScaleArg sc, float* __restrict__ P, int* __restrict__ status) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    char* const buf = reinterpret_cast<char*>(sm);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sm + PLAIN_BUF);   // [0] operand buffer free
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + PLAIN_BUF + 64);
+    const int tile = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+    int ti, tj;
+    upper_tile(tile, gp.nt, ti, tj);
+    const bool diag = ti == tj;
+    const MatPtr mp = p.tab ? p.tab[b] : p.one;
+    const float* __restrict__ Y = (src == SRC_X) ? mp.X : mp.Q;
+    float s = 1.0f;
+    bool scaled = false;
+    if (sc.maxbits) {
+        s = pow2_scale(__uint_as_float(sc.maxbits[b]));
+        scaled = true;
+    } else if (sc.s) {
+        s = sc.s[b];
+        scaled = true;
+    }
+    const int k0 = sp * gp.KS;
+    const int k1 = min(k0 + gp.KS, K);
+    const int nchunks = (k1 - k0 + CHUNK - 1) / CHUNK;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr uint32_t TC = 256;
+    if (warp == 0) tc::tmem_alloc(tmem_slot, TC);
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&bars[0], 1);
+        tc::mbar_fence_init();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t idesc = tc::idesc_tf32_mn(TILE, TILE);
+    const int colA = ti * TILE + 4 * lane, colB = tj * TILE + 4 * lane;
+    const bool inA = colA < n, inB = !diag && colB < n;
+    uint32_t soff[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) soff[i] = tc::swz_mn_off(4 * warp + i, 4 * lane);
+    float4 ra[4], rb[4];
+    auto load = [&](int c) {
+        const int row0 = k0 + c * CHUNK + 4 * warp;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = row0 + i;
+            const float* yr = Y + (long long)row * ld;
+            float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+            if (row < k1) {
+                if (inA) va = __ldg(reinterpret_cast<const float4*>(yr + colA));
+                if (inB) vb = __ldg(reinterpret_cast<const float4*>(yr + colB));
+            }
+            if (scaled) {
+                va.x = __fmul_rn(va.x, s); va.y = __fmul_rn(va.y, s); va.z = __fmul_rn(va.z, s); va.w = __fmul_rn(va.w, s);
+                vb.x = __fmul_rn(vb.x, s); vb.y = __fmul_rn(vb.y, s); vb.z = __fmul_rn(vb.z, s); vb.w = __fmul_rn(vb.w, s);
+            }
+            ra[i] = va;
+            rb[i] = vb;
+        }
+    };
+    double dsq[4] = {0.0, 0.0, 0.0, 0.0};
+    bool ok = true;
+    load(0);
+    for (int c = 0; c < nchunks; ++c) {
+        if (c >= 1) ok = tc::mbar_wait(&bars[0], (uint32_t)((c - 1) & 1));   // the previous chunk's MMAs are done
+        ok = __syncthreads_and(ok);
+        if (!ok) break;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (diag) {
+                dsq[0] = __fma_rn((double)ra[i].x, (double)ra[i].x, dsq[0]);
+                dsq[1] = __fma_rn((double)ra[i].y, (double)ra[i].y, dsq[1]);
+                dsq[2] = __fma_rn((double)ra[i].z, (double)ra[i].z, dsq[2]);
+                dsq[3] = __fma_rn((double)ra[i].w, (double)ra[i].w, dsq[3]);
+            }
+            tc::store2_at(buf, buf + OPND, soff[i], ra[i]);
+            if (!diag) tc::store2_at(buf + 2 * OPND, buf + 3 * OPND, soff[i], rb[i]);
+        }
+        tc::fence_async_smem();
+        if (c + 1 < nchunks) load(c + 1);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            tc::fence_after_sync();
+            const uint32_t abase = tc::smem_u32(buf);
+            const uint32_t bbase = diag ? abase : abase + 2 * OPND;
+#pragma unroll 1
+            for (int k = 0; k < CHUNK / 8; ++k) {
+                const uint32_t acc_in = (c > 0 || k > 0) ? 1u : 0u;
+                const uint64_t ahi = tc::sdesc_mn128b32(abase + 4096 * k, 512, 2048);
+                const uint64_t alo = tc::sdesc_mn128b32(abase + OPND + 4096 * k, 512, 2048);
+                const uint64_t bhi = tc::sdesc_mn128b32(bbase + 4096 * k, 512, 2048);
+                const uint64_t blo = tc::sdesc_mn128b32(bbase + OPND + 4096 * k, 512, 2048);
+                tc::mma_tf32(tmem, ahi, bhi, idesc, acc_in);
+                tc::mma_tf32(tmem + TILE, ahi, blo, idesc, acc_in);
+                tc::mma_tf32(tmem + TILE, alo, bhi, idesc, 1u);
+            }
+            tc::mma_commit(&bars[0]);
+        }
+    }
+    if (ok) ok = __syncthreads_and(tc::mbar_wait(&bars[0], (uint32_t)((nchunks - 1) & 1)));
+    if (ok) {
+        tc::fence_after_sync();
+        const int row = (warp & 3) * 32 + lane;
+        float* ptile = P + ((size_t)(b * gp.S + sp) * gp.tiles + tile) * TILE * TILE;
+        const uint32_t tq = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((warp >> 2) * 64);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            float v[32], w[32];
+            tc::tmem_ld32(tq + 32 * hh, v);
+            tc::tmem_ld32(tq + TILE + 32 * hh, w);
+            tc::tmem_wait_ld();
+            float* out = ptile + (size_t)row * TILE + (warp >> 2) * 64 + 32 * hh;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(out + i) = make_float4(__fadd_rn(v[i], w[i]), __fadd_rn(v[i + 1], w[i + 1]),
+                                                                  __fadd_rn(v[i + 2], w[i + 2]), __fadd_rn(v[i + 3], w[i + 3]));
+        }
+        if (diag) {
+            double* dsum = reinterpret_cast<double*>(buf);   // operand buffer is free: every MMA has completed
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dsum[warp * TILE + 4 * lane + j] = dsq[j];
+            __syncthreads();
+            if (threadIdx.x < TILE) {
+                const int m = threadIdx.x;
+                double t = dsum[m];
+                for (int w2 = 1; w2 < PLAIN_NT / 32; ++w2) t = __dadd_rn(t, dsum[w2 * TILE + m]);
+                ptile[(size_t)m * TILE + m] = __double2float_rn(t);
+            }
+        }
+    } else if (threadIdx.x == 0) {
+        atomicOr(status, ERR_TIMEOUT);
+        tc::mbar_wait(&bars[0], (uint32_t)((nchunks - 1) & 1));
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tmem, TC);
+}
+
 template <int PARTS>
 static cudaError_t launch_parts(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
                                 float* P, int* status, cudaStream_t st) {
@@ -274,8 +424,11 @@ static cudaError_t launch_parts(PtrArg p, Src src, int K, int n, long long ld, i
 
 cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
                            int accurate, float* P, int* status, cudaStream_t st) {
-    return accurate ? launch_parts<3>(p, src, K, n, ld, B, gp, sc, P, status, st)
-                    : launch_parts<2>(p, src, K, n, ld, B, gp, sc, P, status, st);
+    if (accurate) return launch_parts<3>(p, src, K, n, ld, B, gp, sc, P, status, st);
+    cudaError_t e = cudaFuncSetAttribute(k_gram_tc_plain, cudaFuncAttributeMaxDynamicSharedMemorySize, PLAIN_SMEM);
+    if (e != cudaSuccess) return e;
+    k_gram_tc_plain<<<dim3(gp.tiles, gp.S, B), PLAIN_NT, PLAIN_SMEM, st>>>(p, src, K, n, ld, gp, sc, P, status);
+    return cudaGetLastError();
 }
 
 }  // namespace spq

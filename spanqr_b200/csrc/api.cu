@@ -66,7 +66,7 @@ cudaError_t timed(int kind, cudaStream_t st, F&& launch) {
 size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, W, P, total;
+    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, W, maps, P, total;
 };
 
 Layout layout(int K, int r, int B) {
@@ -82,6 +82,7 @@ Layout layout(int K, int r, int B) {
     l.L = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
     l.W = o;       o += (r <= 256) ? al256(trsm_w_bytes(r) * (size_t)B) : 0;
+    l.maps = o;    o += (r <= 256) ? al256((size_t)TMAPS_PER_MATRIX * 128 * B) : 0;
     l.P = o;       o += al256(sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE);
     l.total = o;
     return l;
@@ -117,6 +118,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
     float* Lm = at<float>(ws, l.L);
     float* Li = at<float>(ws, l.Li);
     char* W = at<char>(ws, l.W);
+    char* maps = at<char>(ws, l.maps);
     float* P = at<float>(ws, l.P);
     cudaError_t e;
 #define SPQ_TRY(call)                          \
@@ -124,6 +126,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         if ((e = (call)) != cudaSuccess) return cuda_fail(e); \
     } while (0)
     SPQ_TRY(timed(K_ABSMAX, st, [&] { return launch_absmax(p, K, r, ldx, B, maxbits, st); }));
+    if (r <= 256) SPQ_TRY(timed(K_SETUP, st, [&] { return launch_tmaps(p, K, r, ldx, ldq, B, ws, maps, st); }));
     for (int pass = 0; pass < PASSES; ++pass) {
         const bool first = pass == 0;
         const ScaleArg sc = first ? ScaleArg{maxbits, nullptr} : ScaleArg{nullptr, nullptr};
@@ -138,7 +141,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         }));
         if (r <= 256) SPQ_TRY(timed(K_TRSM_W, st, [&] { return launch_trsm_w(Lm, Li, r, B, W, st); }));
         SPQ_TRY(timed(K_TRSM, st, [&] {
-            return r <= 256 ? launch_trsm_tc(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
+            return r <= 256 ? launch_trsm_tc(p, first ? SRC_X : SRC_Q, K, r, ldq, B, maps, first ? Z : nullptr, sc,
                                              first ? EPS : 0.0f, W, status, st)
                             : launch_trsm(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
                                           first ? EPS : 0.0f, Lm, Li, st);
@@ -332,9 +335,10 @@ int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* 
     PtrArg p{nullptr, MatPtr{X, Y}};
     cudaError_t e = cudaMemsetAsync(at<int>(ws, l.status), 0, sizeof(int), st);
     if (e == cudaSuccess && n <= 256) e = launch_trsm_w(L, Li, n, 1, at<char>(ws, l.W), st);
+    if (e == cudaSuccess && n <= 256) e = launch_tmaps(p, K, n, ldx, ldy, 1, ws, at<char>(ws, l.maps), st);
     if (e == cudaSuccess)
-        e = n <= 256 ? launch_trsm_tc(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f,
-                                      at<char>(ws, l.W), at<int>(ws, l.status), st)
+        e = n <= 256 ? launch_trsm_tc(p, SRC_X, K, n, ldy, 1, at<char>(ws, l.maps), Z, ScaleArg{nullptr, d_s},
+                                      Z ? eps : 0.0f, at<char>(ws, l.W), at<int>(ws, l.status), st)
                      : launch_trsm(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }

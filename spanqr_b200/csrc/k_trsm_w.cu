@@ -1,6 +1,8 @@
 // Operand image of the tensor-core triangular solve: W_jk = -Li_j L_jk (k < j) and W_jj = Li_j, 32 x 32 tiles of the
 // block lower triangle, split into tf32 hi + lo and laid out exactly as the solve's shared-memory operand tiles
-// (K-major, 128B swizzle; 4 KB per part), so the solve copies them in without converting.
+// (K-major, 128B swizzle; 4 KB per part), so the solve copies them in without converting.  Tiles are grouped by block
+// column k (wcol_off): the diagonal tile, then the hi parts of the tiles below it, then their lo parts, so that the
+// tiles one finished block updates arrive in one copy and stack into one N = 32 (nb - 1 - k) operand.
 //
 // The solve's block recurrence  Y_j = (A_j - sum_{k<j} Y_k L_jk^T) Li_j^T  (candidates/tri.py:391-401) is evaluated as
 // Y_j = A_j W_jj^T + sum_{k<j} Y_k W_jk^T: the same operation, with the diagonal-tile inverse applied to the
@@ -13,13 +15,19 @@ namespace spq {
 __global__ void __launch_bounds__(256) k_trsm_w(const float* __restrict__ L_all, const float* __restrict__ Li_all, int n,
                                                 char* __restrict__ W_all) {
     const int t = blockIdx.x, b = blockIdx.y;
-    const int nb = n / TB, ntile = nb * (nb + 1) / 2;
+    const int nb = n / TB;
     int j = 0;
     while ((j + 1) * (j + 2) / 2 <= t) ++j;
     const int k = t - j * (j + 1) / 2;
     const float* L = L_all + (size_t)b * n * n;
     const float* Li = Li_all + (size_t)b * n * TB;
-    char* img = W_all + ((size_t)b * ntile + t) * 2 * 4096;
+    char* col = W_all + (size_t)b * wcol_off(nb, nb) + wcol_off(nb, k);
+    char* hi = col;
+    char* lo = col + 4096;
+    if (k < j) {
+        hi = col + 2 * 4096 + (size_t)(j - k - 1) * 4096;
+        lo = hi + (size_t)(nb - 1 - k) * 4096;
+    }
     __shared__ float sLi[TB][TB + 1], sL[TB][TB + 1];
     for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
         const int r = e / TB, c = e % TB;
@@ -42,7 +50,7 @@ __global__ void __launch_bounds__(256) k_trsm_w(const float* __restrict__ L_all,
             w[i] = -__double2float_rn(acc);
         }
     }
-    tc::store2_at(img, img + 4096, tc::swz_off(r, q), make_float4(w[0], w[1], w[2], w[3]));
+    tc::store2_at(hi, lo, tc::swz_off(r, q), make_float4(w[0], w[1], w[2], w[3]));
 }
 
 cudaError_t launch_trsm_w(const float* L, const float* Li, int n, int B, char* W, cudaStream_t st) {

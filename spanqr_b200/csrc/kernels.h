@@ -1,5 +1,6 @@
 // Host-side launchers of the spanqr kernels (one translation unit per kernel family).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -39,6 +40,15 @@ cudaError_t launch_setup_host(MatPtr* tab, const float* const* hX, float* const*
                               int* status, cudaStream_t st);
 cudaError_t launch_absmax(PtrArg p, int K, int r, long long ldx, int B, uint32_t* maxbits, cudaStream_t st);
 
+// TMA tensor maps of X and of Q per matrix (maps[b * TMAPS_PER_MATRIX + 0 / 1], 128 bytes each), 2-D fp32 tiles of
+// TMAP_BOX_COLS x TMAP_BOX_ROWS; `any` is a 16-byte aligned device address for the host-side templates
+constexpr int TMAPS_PER_MATRIX = 2;
+constexpr int TMAP_BOX_COLS = 32;
+constexpr int TMAP_BOX_ROWS = 128;
+cudaError_t encode_rows(CUtensorMap* m, const void* base, int rows, int cols, long long ld, int box_cols, int box_rows);
+cudaError_t launch_tmaps(PtrArg p, int K, int r, long long ldx, long long ldq, int B, const void* any, char* maps,
+                         cudaStream_t st);
+
 // tensor-core Gram: 128 x 128 tiles, splits of GRAM_TC_SPLIT rows (a multiple of 128); partials
 // P[b][split][tile][128][128]; a bounded wait that runs out ORs 0x10 into *status
 constexpr int GRAM_TC_SPLIT = 512;
@@ -58,11 +68,15 @@ cudaError_t launch_rowsq(const float* G, int n, int B, double* rowsq, cudaStream
 cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, const float* tau_ptr,
                         PassScal* scal, int zero_upper, cudaStream_t st);
 
-// the solve's coefficient image W (W_jj = Li_j, W_jk = -Li_j L_jk, split tf32 tiles), trsm_w_bytes(n) per matrix
+// The solve's coefficient image W (W_jj = Li_j, W_jk = -Li_j L_jk, split tf32 tiles of 4 KB per part), grouped by
+// block column k: [W_kk hi | W_kk lo | W_{k+1..nb-1, k} hi | W_{k+1..nb-1, k} lo]; wcol_off(nb, k) is the group's
+// byte offset, wcol_off(nb, nb) = trsm_w_bytes(n) the size per matrix.
+__host__ __device__ inline size_t wcol_off(int nb, int k) { return (size_t)(k * nb - k * (k - 1) / 2) * 2 * 4096; }
 size_t trsm_w_bytes(int n);
 cudaError_t launch_trsm_w(const float* L, const float* Li, int n, int B, char* W, cudaStream_t st);
-// the same solve on the tensor cores from the image W, n <= 256; a bounded wait that runs out ORs 0x40 into *status
-cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
+// the same solve on the tensor cores from the image W, n <= 256, input rows by the TMA maps (maps: X, 1: Q of matrix
+// b, from launch_tmaps), output to Q; a bounded wait that runs out ORs 0x40 into *status
+cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, const char* maps, const float* Z,
                            ScaleArg sc, float eps, const char* W, int* status, cudaStream_t st);
 
 // Y = (s X + eps Z) L^-T per matrix: input from `src`, output to Q (in place when src == SRC_Q)

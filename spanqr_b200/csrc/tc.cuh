@@ -220,3 +220,49 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 }  // namespace tc
 }  // namespace spq
+
+namespace spq {
+namespace tc {
+// ---- bulk (TMA engine) global -> shared copies, completion counted in bytes on an mbarrier ----
+// The copy engine writes shared memory directly: no registers and no L1 staging, so a CTA that holds most of the
+// SM's shared memory can keep many copies in flight.  Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+}  // namespace tc
+}  // namespace spq
+
+namespace spq {
+namespace tc {
+// ---- tensor-map (TMA) tile loads ----
+// A tensor map written by a kernel (k_tmaps) is made visible to the copy engine by that kernel's release fence; the
+// consumer acquires it once before its first load.
+__device__ __forceinline__ void tmap_acquire(const void* map) {
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(map) : "memory");
+}
+// 2-D tile at coordinates (c0 = column, c1 = row); c0 * 4 bytes must be a multiple of 16; rows past the tensor's end
+// arrive as zeros and still count toward the barrier's bytes
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(smem_dst)), "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+// ---- TMEM stores (one warp: its 32 lanes, 32 consecutive columns) ----
+__device__ __forceinline__ void tmem_st32_zero(uint32_t taddr) {
+    const uint32_t z = 0u;
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+        "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+}  // namespace tc
+}  // namespace spq

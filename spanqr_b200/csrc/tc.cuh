@@ -266,3 +266,35 @@ __device__ __forceinline__ void tmem_st32_zero(uint32_t taddr) {
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 }  // namespace tc
 }  // namespace spq
+
+namespace spq {
+namespace tc {
+// ---- warp-role synchronisation ----
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// named barrier `id` (1..15) over `count` threads (a multiple of 32)
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+}  // namespace tc
+}  // namespace spq
+
+namespace spq {
+namespace tc {
+// named barrier `id` over `count` threads that also ANDs a predicate across them: a group that must leave a loop
+// together (because it meets again at a named barrier) decides with this
+__device__ __forceinline__ bool bar_and(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "barrier.red.and.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+}  // namespace tc
+}  // namespace spq

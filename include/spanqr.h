@@ -15,7 +15,7 @@
  *   - the return value is SPANQR_OK or an error code (spanqr_strerror); nothing is enqueued on an error.
  *
  * Reference interfaces these replace (file:line in oguzeldereli/spanqr):
- *   spanqr_orth_f32          orth.py:13-20 -> candidates/kcholqr.py:112-132 kcholqr_f(X)
+ *   spanqr_orth_f32          orth.py:13-20 -> candidates/kcholqr.py:92-112 kcholqr_f(X)
  *   spanqr_orth_strided_f32  no reference counterpart: a batch of same-shape layers (orth_batched)
  *   spanqr_orth_batched_f32  no reference counterpart: same, from device arrays of matrix pointers
  *   spanqr_orth_ptrs_f32     no reference counterpart: same, from host arrays of matrix pointers
@@ -59,7 +59,7 @@ int spanqr_workspace_bytes(int K, int r, int batch, size_t* bytes);
 /*
  * Q = orth(X).  X [K, r] (leading dimension ldx) is read only; Q [K, r] (ldq) is written.  Z [K, r] (leading
  * dimension r) is the dust: the reference draws it once per shape with torch.randn on the CUDA generator seeded
- * 20261018 and divides each column by its norm (kcholqr.py:103-109); the caller passes it in.
+ * 20261018 and divides each column by its norm (kcholqr.py:83-89); the caller passes it in.
  */
 int spanqr_orth_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z,
                     void* ws, size_t ws_bytes, spanqr_stream_t stream);

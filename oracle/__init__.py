@@ -1,7 +1,7 @@
 """CPU oracle for spanqr's orth(X) -- TEST INFRASTRUCTURE ONLY.
 
 ctypes bindings to ``oracle/liboracle.so`` (built from ``oracle/spanqr_oracle.c`` by ``oracle/Makefile``), a
-plain-C restatement of the reference's ``kcholqr_f`` (candidates/kcholqr.py:112-132) and of its kernels
+plain-C restatement of the reference's ``kcholqr_f`` (candidates/kcholqr.py:92-112) and of its kernels
 (candidates/cuk/chol.cu, candidates/tri.py).  Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
 CPU-baseline leg import this package; the product (``spanqr_b200``) never does.
 
@@ -25,7 +25,7 @@ _ll = ctypes.c_longlong
 _P = ctypes.c_void_p
 
 NSM_B200 = 148
-EPS, ALPHA, TAU, NS = 5e-7, 1e-7, 1e-8, 2          # kcholqr.py:112
+EPS, ALPHA, TAU, NS = 5e-7, 1e-7, 1e-8, 2          # kcholqr.py:92
 
 
 def build(force=False):
@@ -84,7 +84,7 @@ def rsqrt(x):
 
 
 def pow2_scale(m):
-    """kcholqr.py:49-50 _pow2_scale for one fp32 value"""
+    """kcholqr.py:29-30 _pow2_scale for one fp32 value"""
     return np.float32(lib().oracle_pow2_scale(float(np.float32(m))))
 
 
@@ -177,7 +177,7 @@ def num_threads():
 
 
 def dust(K, r, seed=20261018):
-    """a CPU stand-in for the reference's dust (kcholqr.py:103-109 draws it on the CUDA generator): randn on
+    """a CPU stand-in for the reference's dust (kcholqr.py:83-89 draws it on the CUDA generator): randn on
     the CPU generator with the same seed, unit columns.  Tests on CPU use it as an input like any other."""
     import torch
     g = torch.Generator().manual_seed(seed)

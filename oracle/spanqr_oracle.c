@@ -2,7 +2,7 @@
  * CPU ORACLE for spanqr's orth(X) -- TEST INFRASTRUCTURE ONLY.
  *
  * This file restates, in plain C, the algorithm of the reference's GPU path
- *   orth.py:13-20 -> candidates/kcholqr.py:112-132 (kcholqr_f)
+ *   orth.py:13-20 -> candidates/kcholqr.py:92-112 (kcholqr_f)
  * so that tests can check the CUDA product against it, and so that bench.py can time it as the CPU
  * baseline.  Nothing in the product (spanqr_b200/, libspanqr.so) links, loads or calls this file; only
  * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg do.
@@ -57,7 +57,7 @@ float oracle_rsqrt(float x) {
 }
 
 /* ---------------------------------------------------------------------------------------------------
- * kcholqr.py:49-50  _pow2_scale(m) = where(m > 0, exp2(-round(log2(clamp_min(m, 1e-38)))), 1)
+ * kcholqr.py:29-30  _pow2_scale(m) = where(m > 0, exp2(-round(log2(clamp_min(m, 1e-38)))), 1)
  * As in the reference, log2 is rounded to fp32 first and round() is half-to-even on that fp32 value: near
  * 2^(k + 1/2) with large |k| the fp32 log2 is exactly k + 1/2 and the even neighbour wins.  The fp32 log2 is
  * the correctly rounded one (log2 in fp64, then rounded), which is what torch's CPU log2 returns there.
@@ -72,7 +72,7 @@ float oracle_pow2_scale(float m) {
     return ldexpf(1.0f, -(int)k);
 }
 
-/* torch.linalg.vector_norm(X, ord=inf): max |x|, NaN-propagating (kcholqr.py:122) */
+/* torch.linalg.vector_norm(X, ord=inf): max |x|, NaN-propagating (kcholqr.py:102) */
 float oracle_absmax(const float* X, long long K, int r, long long ldx) {
     float m = 0.0f;
     int nan = 0;
@@ -145,7 +145,7 @@ void oracle_gram_kahan(const float* Y, int K, int n, long long ldy, float s, int
     free(At);
 }
 
-/* Y^T Y as a plain fp32 GEMM (kcholqr.py:126 and :40, cuBLAS SGEMM; its order is not specified):
+/* Y^T Y as a plain fp32 GEMM (kcholqr.py:106 and :20, cuBLAS SGEMM; its order is not specified):
  * FMA chains over 32-row chunks, chunk sums added in fp32 in order. */
 void oracle_gram_plain(const float* Y, int K, int n, long long ldy, float* G) {
     float* At = transpose_scaled(Y, K, n, ldy, 1.0f, 0);
@@ -321,7 +321,7 @@ void oracle_trsm(const float* X, long long ldx, const float* Z, float s, int has
     }
 }
 
-/* Frobenius norm (torch.linalg.matrix_norm, kcholqr.py:127): squares summed in fp64, one row at a time (columns
+/* Frobenius norm (torch.linalg.matrix_norm, kcholqr.py:107): squares summed in fp64, one row at a time (columns
  * in order), then the row sums in order; rounded to fp32 after the square root. */
 float oracle_fro(const float* G, int n) {
     double tot = 0.0;
@@ -337,7 +337,7 @@ float oracle_fro(const float* G, int n) {
 }
 
 /* ---------------------------------------------------------------------------------------------------
- * kcholqr.py:36-43 _ns_mm: Newton-Schulz as a correction, Y <- Y + Y D with D = 0.5 (I - Y^T Y).
+ * kcholqr.py:16-23 _ns_mm: Newton-Schulz as a correction, Y <- Y + Y D with D = 0.5 (I - Y^T Y).
  * The reference takes step i < n-1's Gram from cuBLAS SGEMM (order unspecified) and the last step's from the
  * Kahan split Gram (gram_split, bt=64); here every step uses the split Gram (at least as accurate, fixed order).
  * D = eye.sub_(G).mul_(0.5) rounds twice; addmm(Y, Y, D) adds the fp32 product to Y.
@@ -374,11 +374,11 @@ void oracle_ns(float* Y, int K, int n, int steps, int nsm) {
 }
 
 /* ---------------------------------------------------------------------------------------------------
- * kcholqr.py:112-132 kcholqr_f(X, eps=5e-7, alpha=1e-7, tau=1e-8, ns=2):
+ * kcholqr.py:92-112 kcholqr_f(X, eps=5e-7, alpha=1e-7, tau=1e-8, ns=2):
  *   s = pow2_scale(max|X|); 3 passes of {G = gram (pass 0: Kahan split Gram of s X, dust excluded;
  *   later: the reference's cuBLAS SGEMM, here the same split Gram), nrm = ||G||_F, G_ii += alpha nrm, (L, Li) = chol32(G, tau nrm + 1e-30),
  *   Y = trsm(Y, L, Li) with s X + eps Z on pass 0}; then _ns_mm(Y, ns).
- * Z: the dust, K x r, unit columns (kcholqr.py:103-109; the caller builds it).
+ * Z: the dust, K x r, unit columns (kcholqr.py:83-89; the caller builds it).
  * Returns 0, or 1 for an unsupported shape (r % 32 != 0; the reference then falls back to Householder).
  * ------------------------------------------------------------------------------------------------- */
 int oracle_kcholqr_f(const float* X, long long ldx, const float* Z, int K, int r, float eps, float alpha,
@@ -410,7 +410,7 @@ int oracle_kcholqr_f(const float* X, long long ldx, const float* Z, int K, int r
     return 0;
 }
 
-/* orth(X) with the reference's constants (kcholqr.py:112) */
+/* orth(X) with the reference's constants (kcholqr.py:92) */
 int oracle_orth(const float* X, long long ldx, const float* Z, int K, int r, int nsm, float* Q) {
     return oracle_kcholqr_f(X, ldx, Z, K, r, 5e-7f, 1e-7f, 1e-8f, 2, nsm, Q);
 }

@@ -1,11 +1,11 @@
-"""orth(X): the drop-in for spanqr's `orth` (orth.py:13-20 -> candidates/kcholqr.py:112-132, kcholqr_f).
+"""orth(X): the drop-in for spanqr's `orth` (orth.py:13-20 -> candidates/kcholqr.py:92-112, kcholqr_f).
 
     from spanqr_b200 import orth
     Q = orth(X)      # X: fp32 CUDA [K, r] -> Q: fp32 CUDA [K, r], Q^T Q = I, span(Q) = span(X)
 
 Every call runs on libspanqr's CUDA kernels on the current stream, with no host synchronisation.  There is no
 fallback: an unsupported shape raises (the reference silently falls back to torch.linalg.qr for r % 32 != 0,
-kcholqr.py:118-119, and routes r > 512 to block Gram-Schmidt, orth.py:18-19).
+kcholqr.py:98-99, and routes r > 512 to block Gram-Schmidt, orth.py:18-19).
 """
 import threading
 
@@ -15,7 +15,7 @@ from . import _lib
 
 TB = 32               # tile width (candidates/kchol.py:9)
 MAX_R = 512
-DUST_SEED = 20261018  # candidates/kcholqr.py:106
+DUST_SEED = 20261018  # candidates/kcholqr.py:86
 
 _Z = {}
 _WS = {}
@@ -23,7 +23,7 @@ _lock = threading.Lock()
 
 
 def zdust(K, r, device):
-    """The dust Z of kcholqr.py:103-109: torch.randn(K, r) on the device's generator seeded 20261018, each column
+    """The dust Z of kcholqr.py:83-89: torch.randn(K, r) on the device's generator seeded 20261018, each column
     divided by its norm; cached per (K, r, device).  Drawn with torch on the same device as the reference draws it,
     so both see the same Z."""
     device = torch.device(device)

@@ -1,6 +1,6 @@
 // C ABI of libspanqr: argument checks, workspace layout and the orth pass sequence.
 //
-// orth(X) (candidates/kcholqr.py:112-132, kcholqr_f with eps 5e-7, alpha 1e-7, tau 1e-8, ns 2) as a stream-ordered
+// orth(X) (candidates/kcholqr.py:92-112, kcholqr_f with eps 5e-7, alpha 1e-7, tau 1e-8, ns 2) as a stream-ordered
 // sequence of kernels; no host synchronisation, no device allocation.  Between passes Y lives in Q (the row-block
 // kernels run in place), so the workspace holds only r x r matrices and the Gram partials.
 #include <cstdint>
@@ -16,9 +16,9 @@ using namespace spq;
 
 namespace {
 
-constexpr float EPS = 5e-7f;    // dust weight, pass 1 (kcholqr.py:112)
-constexpr int NS_STEPS = 2;     // Newton-Schulz polish steps (kcholqr.py:112)
-constexpr int PASSES = 3;       // shifted Cholesky-QR passes (kcholqr.py:125)
+constexpr float EPS = 5e-7f;    // dust weight, pass 1 (kcholqr.py:92)
+constexpr int NS_STEPS = 2;     // Newton-Schulz polish steps (kcholqr.py:92)
+constexpr int PASSES = 3;       // shifted Cholesky-QR passes (kcholqr.py:105)
 
 thread_local char g_cuda_err[256] = "";
 

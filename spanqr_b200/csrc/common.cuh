@@ -39,7 +39,7 @@ __device__ __forceinline__ float det_rsqrt(float x) {
     return __fmaf_rn(__fmul_rn(0.5f, y), e, y);
 }
 
-// kcholqr.py:49-50 _pow2_scale: 2^-round(log2 max(m, 1e-38)), 1 when m is 0 or NaN, 0 when m is inf.
+// kcholqr.py:29-30 _pow2_scale: 2^-round(log2 max(m, 1e-38)), 1 when m is 0 or NaN, 0 when m is inf.
 // log2 is rounded to fp32 first (fp64 log2, then rounded) and round() is half-to-even on that value,
 // as torch computes it.
 __device__ __forceinline__ float pow2_scale(float m) {

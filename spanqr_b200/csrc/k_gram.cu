@@ -2,7 +2,7 @@
 //
 // k_gram_reduce: G = fp64 sum of the split partials of k_gram_tc (128 x 128 tiles of the upper triangle) in split
 // order, rounded to fp32 and mirrored, as tri.py:375 sums its splits (P.sum(0, float64).float()); with make_D it
-// writes D = 0.5 (I - G) instead (kcholqr.py:41).
+// writes D = 0.5 (I - G) instead (kcholqr.py:21).
 #include "kernels.h"
 
 namespace spq {

@@ -1,4 +1,4 @@
-// Newton-Schulz update Y <- Y + Y D (candidates/kcholqr.py:42, torch.addmm(Y, Y, D)) on the tcgen05 tensor cores.
+// Newton-Schulz update Y <- Y + Y D (candidates/kcholqr.py:22, torch.addmm(Y, Y, D)) on the tcgen05 tensor cores.
 //
 // One CTA = 128 rows of one matrix and all N = n output columns (n <= 256; wider matrices use k_ns_update, which
 // holds whole rows in shared memory).  The contraction runs over the n columns of Y in chunks of 32: per chunk the 256

@@ -40,7 +40,7 @@ __global__ void k_setup_chunk(MatPtr* tab, PtrChunk c, int b0, int nb, uint32_t*
     if (b0 == 0 && i == 0) status[0] = 0;
 }
 
-// max |x| over X[b] (K x r, leading dimension ldx) as bits; NaN wins (kcholqr.py:122 vector_norm(ord=inf)).
+// max |x| over X[b] (K x r, leading dimension ldx) as bits; NaN wins (kcholqr.py:102 vector_norm(ord=inf)).
 // The maximum is order-independent, so the atomic combine is deterministic.
 __global__ void __launch_bounds__(256) k_absmax(PtrArg p, int K, int r, long long ldx, uint32_t* maxbits) {
     const int b = blockIdx.y;

@@ -5,7 +5,7 @@
 //
 // trsm follows candidates/tri.py:378-403 (_trsm_f_kernel): 32-column blocks j in order; acc = s x (+ eps z); for each
 // earlier block k, acc -= (Y_k L[j, k]^T) with that dot as one FMA chain; then Y_j = acc Li_j^T.
-// ns_update follows candidates/kcholqr.py:42 (torch.addmm(Y, Y, D)): y + (sum_a y_a D[a, c]), the sum an FMA chain.
+// ns_update follows candidates/kcholqr.py:22 (torch.addmm(Y, Y, D)): y + (sum_a y_a D[a, c]), the sum an FMA chain.
 // Thread map: 256 threads = 32 row pairs x 8 column groups of 4; shared rows padded to n + 1 floats (no bank
 // conflicts for the column-group reads).
 #include "kernels.h"

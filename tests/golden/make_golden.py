@@ -5,7 +5,7 @@ Run in a container that has the reference checkout (it is never read at test tim
     python tests/golden/make_golden.py --ref /path/to/spanqr
 
 What runs, and what is substituted:
-  * the reference's own orchestration ``candidates.kcholqr.kcholqr_f`` (kcholqr.py:112-132), its ``_pow2_scale``,
+  * the reference's own orchestration ``candidates.kcholqr.kcholqr_f`` (kcholqr.py:92-112), its ``_pow2_scale``,
     ``_zdust`` (on the CPU generator, seed 20261018), ``_ns_mm``, and its Triton kernels ``tri.gram_f`` /
     ``tri.gram_split`` / ``tri._trsm_f_kernel`` executed by Triton's CPU interpreter (TRITON_INTERPRET=1);
   * the reference's test-matrix builders ``qrbench.gen`` (cases and seed formula, gen.py:171-182), kept on CPU;

@@ -28,9 +28,9 @@ int cuda_fail(cudaError_t e) {
 }
 
 // ---- optional per-kernel timing (spanqr_timing_*) ----
-enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_COUNT };
+enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_GRAM_ACC, K_COUNT };
 const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce", "k_rowsq",
-                                         "k_chol", "k_trsm_w", "k_trsm", "k_ns_update"};
+                                         "k_chol", "k_trsm_w", "k_trsm", "k_ns_update", "k_gram_tc_acc"};
 struct TimedLaunch {
     int kind;
     cudaEvent_t a, b;
@@ -130,9 +130,12 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
     for (int pass = 0; pass < PASSES; ++pass) {
         const bool first = pass == 0;
         const ScaleArg sc = first ? ScaleArg{maxbits, nullptr} : ScaleArg{nullptr, nullptr};
+        // every pass uses the two-way split (passes 2 and 3 are plain SGEMMs in the reference; pass 1's compensated
+        // gram_f is matched closely enough by it: the robustness and span tests pass either way)
         SPQ_TRY(timed(K_GRAM, st, [&] {
-            return launch_gram_tc(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, first ? 1 : 0, P,
-                                  status, st);
+            return r <= 256 ? launch_gram_ws(p, first ? SRC_X : SRC_Q, K, r, B, gp, maps, sc, P, status, st)
+                            : launch_gram_tc(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, 0, P, status,
+                                             st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 0, G, st); }));
         SPQ_TRY(timed(K_ROWSQ, st, [&] { return launch_rowsq(G, r, B, rowsq, st); }));
@@ -148,9 +151,14 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         }));
     }
     for (int it = 0; it < NS_STEPS; ++it) {
-        SPQ_TRY(timed(K_GRAM, st, [&] {
-            return launch_gram_tc(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, it == NS_STEPS - 1 ? 1 : 0, P,
-                                  status, st);
+        // the last polish step's Gram decides Q's final orthogonality (and with it the span error on the dominant
+        // directions): it keeps the exact three-way split and fp64 drains every 32 rows (gram_split, kcholqr.py:20)
+        const bool last = it == NS_STEPS - 1;
+        SPQ_TRY(timed(last ? K_GRAM_ACC : K_GRAM, st, [&] {
+            return (r <= 256 && !last)
+                       ? launch_gram_ws(p, SRC_Q, K, r, B, gp, maps, ScaleArg{nullptr, nullptr}, P, status, st)
+                       : launch_gram_tc(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, last ? 1 : 0, P, status,
+                                        st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, st); }));
         // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel

@@ -1,5 +1,5 @@
-// Per-matrix TMA tensor maps of the row-major X and Q of every matrix in a call (2-D fp32, tiles of 32 columns x 128
-// rows, rows past K read as zeros).  The host encodes one template per operand (cuTensorMapEncodeTiled, fetched from
+// Per-matrix TMA tensor maps of the row-major X and Q of every matrix in a call (2-D fp32; tiles of 32 columns x 128
+// rows for the solve, 128 columns x 32 rows for the Gram; rows past K and columns past r read as zeros).  The host encodes one template per operand (cuTensorMapEncodeTiled, fetched from
 // the driver at run time); k_tmaps copies it once per matrix into the workspace and patches in that matrix's address
 // with tensormap.replace, so batched calls whose pointers live only on the device get maps too.
 #include <cudaTypedefs.h>
@@ -40,31 +40,36 @@ cudaError_t encode_rows(CUtensorMap* m, const void* base, int rows, int cols, lo
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-__global__ void k_tmaps(PtrArg p, int B, const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tq,
-                        char* __restrict__ maps) {
+struct TmapTemplates {
+    CUtensorMap m[TMAPS_PER_MATRIX];
+};
+
+__global__ void k_tmaps(PtrArg p, int B, const __grid_constant__ TmapTemplates t, char* __restrict__ maps) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const MatPtr mp = p.tab ? p.tab[b] : p.one;
     int4* d = reinterpret_cast<int4*>(maps + (size_t)b * TMAPS_PER_MATRIX * 128);
-    const int4* sx = reinterpret_cast<const int4*>(&tx);
-    const int4* sq = reinterpret_cast<const int4*>(&tq);
+    const int4* src = reinterpret_cast<const int4*>(&t);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        d[i] = sx[i];
-        d[8 + i] = sq[i];
+    for (int i = 0; i < 8 * TMAPS_PER_MATRIX; ++i) d[i] = src[i];
+#pragma unroll
+    for (int m = 0; m < TMAPS_PER_MATRIX; ++m) {
+        const void* a = (m == TMAP_X || m == TMAP_GX) ? static_cast<const void*>(mp.X) : static_cast<const void*>(mp.Q);
+        asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(d + 8 * m), "l"(a)
+                     : "memory");
     }
-    asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(d), "l"(mp.X) : "memory");
-    asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(d + 8), "l"(mp.Q) : "memory");
     asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
 }
 
 cudaError_t launch_tmaps(PtrArg p, int K, int r, long long ldx, long long ldq, int B, const void* any, char* maps,
                          cudaStream_t st) {
-    alignas(64) CUtensorMap tx, tq;
-    cudaError_t e = encode_rows(&tx, any, K, r, ldx, TMAP_BOX_COLS, TMAP_BOX_ROWS);
-    if (e == cudaSuccess) e = encode_rows(&tq, any, K, r, ldq, TMAP_BOX_COLS, TMAP_BOX_ROWS);
+    alignas(64) TmapTemplates t;
+    cudaError_t e = encode_rows(&t.m[TMAP_X], any, K, r, ldx, TMAP_BOX_COLS, TMAP_BOX_ROWS);
+    if (e == cudaSuccess) e = encode_rows(&t.m[TMAP_Q], any, K, r, ldq, TMAP_BOX_COLS, TMAP_BOX_ROWS);
+    if (e == cudaSuccess) e = encode_rows(&t.m[TMAP_GX], any, K, r, ldx, GRAM_BOX_COLS, GRAM_BOX_ROWS);
+    if (e == cudaSuccess) e = encode_rows(&t.m[TMAP_GQ], any, K, r, ldq, GRAM_BOX_COLS, GRAM_BOX_ROWS);
     if (e != cudaSuccess) return e;
-    k_tmaps<<<(B + 127) / 128, 128, 0, st>>>(p, B, tx, tq, maps);
+    k_tmaps<<<(B + 127) / 128, 128, 0, st>>>(p, B, t, maps);
     return cudaGetLastError();
 }
 

@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
     } else {
         // ---------------- copy warp ----------------
         if (lane == 0) {
-            const void* amap = maps + ((size_t)b * TMAPS_PER_MATRIX + (src == SRC_X ? 0 : 1)) * 128;
+            const void* amap = maps + ((size_t)b * TMAPS_PER_MATRIX + (src == SRC_X ? TMAP_X : TMAP_Q)) * 128;
             const char* Wimg = W_all + (size_t)b * wcol_off(nb, nb);
             tc::tmap_acquire(amap);
             int n_a[2] = {0, 0}, n_wd[2] = {0, 0}, n_wt[2] = {0, 0};

@@ -40,11 +40,16 @@ cudaError_t launch_setup_host(MatPtr* tab, const float* const* hX, float* const*
                               int* status, cudaStream_t st);
 cudaError_t launch_absmax(PtrArg p, int K, int r, long long ldx, int B, uint32_t* maxbits, cudaStream_t st);
 
-// TMA tensor maps of X and of Q per matrix (maps[b * TMAPS_PER_MATRIX + 0 / 1], 128 bytes each), 2-D fp32 tiles of
-// TMAP_BOX_COLS x TMAP_BOX_ROWS; `any` is a 16-byte aligned device address for the host-side templates
-constexpr int TMAPS_PER_MATRIX = 2;
+// TMA tensor maps per matrix (128 bytes each, maps + (b * TMAPS_PER_MATRIX + m) * 128), 2-D fp32:
+//   m = TMAP_X, TMAP_Q    tiles of TMAP_BOX_COLS x TMAP_BOX_ROWS (32 columns x 128 rows: one solve block)
+//   m = TMAP_GX, TMAP_GQ  tiles of GRAM_BOX_COLS x GRAM_BOX_ROWS (128 columns x 32 rows: one Gram chunk)
+// `any` is a 16-byte aligned device address for the host-side templates.
+constexpr int TMAPS_PER_MATRIX = 4;
+enum { TMAP_X = 0, TMAP_Q = 1, TMAP_GX = 2, TMAP_GQ = 3 };
 constexpr int TMAP_BOX_COLS = 32;
 constexpr int TMAP_BOX_ROWS = 128;
+constexpr int GRAM_BOX_COLS = 128;
+constexpr int GRAM_BOX_ROWS = 32;
 cudaError_t encode_rows(CUtensorMap* m, const void* base, int rows, int cols, long long ld, int box_cols, int box_rows);
 cudaError_t launch_tmaps(PtrArg p, int K, int r, long long ldx, long long ldq, int B, const void* any, char* maps,
                          cudaStream_t st);
@@ -56,6 +61,10 @@ GramPlan gram_tc_plan(int K, int n);
 // accurate: exact three-way split and six products (the reference's compensated Grams); else two-way, three products
 cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
                            int accurate, float* P, int* status, cudaStream_t st);
+// the two-way-split Gram for n <= 256, warp-specialised and fed by TMA (maps from launch_tmaps): one CTA per 128-row
+// panel of G and split, N = n - 128 i columns wide; same partial layout; a bounded wait that runs out ORs 0x10
+cudaError_t launch_gram_ws(PtrArg p, Src src, int K, int n, int B, const GramPlan& gp, const char* maps, ScaleArg sc,
+                           float* P, int* status, cudaStream_t st);
 
 // G[b] (n x n, both triangles) = fp64 sum over splits; with make_D, D = 0.5 (I - G) instead
 cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G,

@@ -48,6 +48,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
     return true;
 }
 
+// The same wait for a thread off the critical path: it sleeps between polls, so that warps sharing its SM
+// sub-partition keep their issue slots.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
+                                                uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(sleep_ns);
+        if (globaltimer() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+
 // ---- proxy and tcgen05 ordering fences ----
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

@@ -83,7 +83,10 @@ Layout layout(int K, int r, int B) {
     l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
     l.W = o;       o += (r <= 256) ? al256(trsm_w_bytes(r) * (size_t)B) : 0;
     l.maps = o;    o += (r <= 256) ? al256((size_t)TMAPS_PER_MATRIX * 128 * B) : 0;
-    l.P = o;       o += al256(sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE);
+    // the Gram's split partials; the polish step's D image reuses them once they are reduced
+    size_t pbytes = sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE;
+    if (r <= 256 && ns_dimg_bytes(r) * B > pbytes) pbytes = ns_dimg_bytes(r) * B;
+    l.P = o;       o += al256(pbytes);
     l.total = o;
     return l;
 }
@@ -163,7 +166,8 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, st); }));
         // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel
         SPQ_TRY(timed(K_NS, st, [&] {
-            return r <= 256 ? launch_ns_tc(p, K, r, ldq, B, G, status, st) : launch_ns_update(p, K, r, ldq, B, G, st);
+            return r <= 256 ? launch_ns_ws(p, K, r, ldq, B, G, maps, reinterpret_cast<char*>(P), status, st)
+                            : launch_ns_update(p, K, r, ldq, B, G, st);
         }));
     }
 #undef SPQ_TRY

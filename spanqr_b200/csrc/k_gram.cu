@@ -7,26 +7,55 @@
 
 namespace spq {
 
+// One CTA = a strip of 32 rows of one upper tile: the fp64 sums of the strip go to shared memory, then to G row by row
+// (coalesced) and, transposed, column by column (also coalesced).  In a diagonal tile the tensor cores give (a, c)
+// and (c, a) from the same products in different roles, which need not round alike: the upper element alone defines
+// both, so G is exactly symmetric.
+constexpr int RSTRIP = 32;
+
 __global__ void __launch_bounds__(256) k_gram_reduce(const float* __restrict__ P, int n, GramPlan gp, int make_D,
                                                      float* __restrict__ G) {
-    const int tile = blockIdx.x, b = blockIdx.y;
+    constexpr int T = GRAM_TILE;
+    const int tile = blockIdx.x / (T / RSTRIP), r0 = (blockIdx.x % (T / RSTRIP)) * RSTRIP, b = blockIdx.y;
     int ti, tj;
     upper_tile(tile, gp.nt, ti, tj);
-    float* Gb = G + (size_t)b * n * n;
-    constexpr int T = GRAM_TILE;
-    for (int e = threadIdx.x; e < T * T; e += blockDim.x) {
-        const int a = ti * T + e / T, c = tj * T + e % T;
-        if (a >= n || c >= n) continue;
-        // in a diagonal tile the tensor cores give (a, c) and (c, a) from the same products in different roles,
-        // which need not round alike: the upper element alone defines both, so G is exactly symmetric
-        if (ti == tj && a > c) continue;
-        double t = 0.0;
-        const float* src = P + (size_t)b * gp.S * gp.tiles * (T * T) + (size_t)tile * (T * T) + e;
-        for (int sp = 0; sp < gp.S; ++sp) t = __dadd_rn(t, (double)src[(size_t)sp * gp.tiles * (T * T)]);
-        float g = __double2float_rn(t);
-        if (make_D) g = __fmul_rn(__fsub_rn(a == c ? 1.0f : 0.0f, g), 0.5f);
-        Gb[(size_t)a * n + c] = g;
-        Gb[(size_t)c * n + a] = g;
+    const bool diag = ti == tj;
+    __shared__ float S[RSTRIP][T + 1];
+    const float* src = P + (size_t)b * gp.S * gp.tiles * (T * T) + (size_t)tile * (T * T) + (size_t)r0 * T;
+    const size_t split_stride = (size_t)gp.tiles * (T * T);
+    // 32 x 128 sums, a float4 of one row per thread and step
+    for (int q = threadIdx.x; q < RSTRIP * T / 4; q += blockDim.x) {
+        const int r = q / (T / 4), c = 4 * (q % (T / 4));
+        double t0 = 0.0, t1 = 0.0, t2 = 0.0, t3 = 0.0;
+        for (int sp = 0; sp < gp.S; ++sp) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + sp * split_stride + (size_t)r * T + c));
+            t0 = __dadd_rn(t0, (double)v.x);
+            t1 = __dadd_rn(t1, (double)v.y);
+            t2 = __dadd_rn(t2, (double)v.z);
+            t3 = __dadd_rn(t3, (double)v.w);
+        }
+        const int a = ti * T + r0 + r;
+        float g[4] = {__double2float_rn(t0), __double2float_rn(t1), __double2float_rn(t2), __double2float_rn(t3)};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (make_D) g[i] = __fmul_rn(__fsub_rn(a == tj * T + c + i ? 1.0f : 0.0f, g[i]), 0.5f);
+            S[r][c + i] = g[i];
+        }
+    }
+    __syncthreads();
+    // rows: G[a][c]; in a diagonal tile only c >= a
+    for (int e = threadIdx.x; e < RSTRIP * T; e += blockDim.x) {
+        const int r = e / T, c = e % T;
+        const int a = ti * T + r0 + r, cg = tj * T + c;
+        if (a >= n || cg >= n || (diag && cg < a)) continue;
+        G[(size_t)b * n * n + (size_t)a * n + cg] = S[r][c];
+    }
+    // columns: G[c][a]; in a diagonal tile only c > a
+    for (int e = threadIdx.x; e < RSTRIP * T; e += blockDim.x) {
+        const int c = e / RSTRIP, r = e % RSTRIP;
+        const int a = ti * T + r0 + r, cg = tj * T + c;
+        if (a >= n || cg >= n || (diag && cg <= a)) continue;
+        G[(size_t)b * n * n + (size_t)cg * n + a] = S[r][c];
     }
 }
 
@@ -47,7 +76,7 @@ __global__ void __launch_bounds__(128) k_rowsq(const float* __restrict__ G, int 
 
 cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G,
                                cudaStream_t st) {
-    k_gram_reduce<<<dim3(gp.tiles, B), 256, 0, st>>>(P, n, gp, make_D, G);
+    k_gram_reduce<<<dim3(gp.tiles * (GRAM_TILE / RSTRIP), B), 256, 0, st>>>(P, n, gp, make_D, G);
     return cudaGetLastError();
 }
 

@@ -305,24 +305,19 @@ def main():
     # end to end through the public API: pinned host inputs of this rank's share in, its results out
     e2e = None
     if not a.no_e2e:
-        hosts = {i: Xs[i].cpu().pin_memory() for i in range(B) if owner[i] == rank}
-        hq = {i: torch.empty_like(hosts[i]).pin_memory() for i in hosts}
-        h2d = sum(h.numel() * 4 for h in hosts.values())
+        # every rank passes the whole list (host copies of all inputs) and gets its own share back in pinned memory
+        hosts = [Xs[i].cpu().pin_memory() if owner[i] == rank else torch.zeros(1, 1).expand(Xs[i].shape)
+                 for i in range(B)]
+        hq = [torch.empty(Xs[i].shape, dtype=torch.float32).pin_memory() if owner[i] == rank else None
+              for i in range(B)]
+        h2d = sum(hosts[i].numel() * 4 for i in range(B) if owner[i] == rank)
         for _ in range(max(1, a.warmup)):
-            for i, h in hosts.items():
-                Xs[i].copy_(h, non_blocking=True)
-            Qs = orth_batched(Xs)
-            for i in hosts:
-                hq[i].copy_(Qs[i], non_blocking=True)
+            orth_batched(hosts, gather=False, out=hq)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(a.steps):
-            for i, h in hosts.items():
-                Xs[i].copy_(h, non_blocking=True)
-            Qs = orth_batched(Xs)
-            for i in hosts:
-                hq[i].copy_(Qs[i], non_blocking=True)
+            orth_batched(hosts, gather=False, out=hq)
         e1.record(stream)
         barrier()
         ems = dist_max(e0.elapsed_time(e1), device)

@@ -9,12 +9,18 @@ matrices are partitioned by cost K * r with a deterministic greedy (largest firs
 the lower rank); each rank computes its share into its slab of one output buffer laid out owner by owner; then the
 slabs are exchanged over NCCL (all_gather_into_tensor when the slabs are equal, else one broadcast per owner), so every
 rank returns every Q.  With gather=False each rank returns only its own Qs (None elsewhere).
+
+Host-resident matrices (CPU tensors, pinned for the copies to overlap): the batch is cut into chunks, and per chunk the
+copy in, the orth and the copy out run on three streams of the current device with two device buffers in turn, so
+the PCIe transfers in both directions overlap each other and the kernels.  Results land in `out` (pinned CPU
+tensors) or in newly allocated pinned tensors; under torch.distributed each rank computes and returns its own share
+(gather=False).
 """
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from .core import check_input, aligned, zdust, workspace
+from .core import check_input, aligned, zdust, workspace, TB, MAX_R
 
 
 def partition(costs, world):
@@ -101,10 +107,85 @@ def _run_local(Xs, Qs):
         _run_group(xs, qs, stream)
 
 
-def orth_batched(Xs, *, gather=True, group=None):
+def _check_host(X, name):
+    if not torch.is_tensor(X) or X.dim() != 2 or X.dtype != torch.float32 or X.is_cuda:
+        raise TypeError(f"{name} must be a 2-D fp32 CPU tensor")
+    K, r = X.shape
+    if r % TB or r < TB or r > MAX_R or K < r:
+        raise ValueError(f"unsupported shape {K}x{r}: r must be a multiple of {TB} in [{TB}, {MAX_R}] and K >= r")
+
+
+def _run_host(Xs, Qs, device, chunks):
+    """Qs[i] = orth(Xs[i]) for CPU tensors, copies in and out overlapped with the kernels (see the module docstring)"""
+    cur = torch.cuda.current_stream(device)
+    s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
+    for s in (s_in, s_cmp, s_out):
+        s.wait_stream(cur)
+    groups = {}
+    for i, x in enumerate(Xs):
+        groups.setdefault(tuple(x.shape), []).append(i)
+    last = None
+    for (K, r), idx in groups.items():
+        zdust(K, r, device)   # drawn on the current stream, which the three streams follow
+        nch = max(1, min(chunks, len(idx)))
+        step = -(-len(idx) // nch)
+        parts = [idx[k:k + step] for k in range(0, len(idx), step)]
+        din = [torch.empty((step, K, r), dtype=torch.float32, device=device) for _ in range(2)]
+        dout = [torch.empty((step, K, r), dtype=torch.float32, device=device) for _ in range(2)]
+        for t in din + dout:
+            for s in (s_in, s_cmp, s_out):
+                t.record_stream(s)
+        ev_out = []
+        for k, part in enumerate(parts):
+            slot = k % 2
+            with torch.cuda.stream(s_in):
+                if k >= 2:
+                    s_in.wait_event(ev_out[k - 2])   # chunk k-2 is computed and copied out: its buffers are free
+                for j, i in enumerate(part):
+                    din[slot][j].copy_(Xs[i], non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(ev_in)
+                if k >= 2:
+                    s_cmp.wait_event(ev_out[k - 2])
+                _run_group([din[slot][j] for j in range(len(part))], [dout[slot][j] for j in range(len(part))], s_cmp)
+                ev_cmp = torch.cuda.Event()
+                ev_cmp.record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_cmp)
+                for j, i in enumerate(part):
+                    Qs[i].copy_(dout[slot][j], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_out)
+                ev_out.append(e)
+        last = ev_out[-1]
+    if last is not None:
+        cur.wait_event(last)   # work on the caller's stream after this call sees every result
+
+
+def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=8):
     """Q_i = orth(X_i) for every matrix.  Xs: a list of fp32 CUDA [K_i, r_i] tensors on one device, or one
     [B, K, r] tensor.  Returns a list of Qs (a [B, K, r] tensor for a tensor input).  Under torch.distributed the
-    work is split across the ranks of `group` (default: the world) and the results all-gathered (gather=True)."""
+    work is split across the ranks of `group` (default: the world) and the results all-gathered (gather=True).
+    A list of CPU tensors runs on the current CUDA device with the copies overlapped (`chunks` pieces) and returns CPU
+    tensors (`out`, if given); under torch.distributed that needs gather=False."""
+    if not torch.is_tensor(Xs) and len(Xs) and torch.is_tensor(Xs[0]) and not Xs[0].is_cuda:
+        Xs = list(Xs)
+        for i, x in enumerate(Xs):
+            _check_host(x, f"Xs[{i}]")
+        distributed = dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1
+        if distributed and gather:
+            raise ValueError("CPU inputs under torch.distributed: pass gather=False (each rank gets its own share)")
+        world = dist.get_world_size(group) if distributed else 1
+        rank = dist.get_rank(group) if distributed else 0
+        owner = partition([x.shape[0] * x.shape[1] for x in Xs], world)
+        if out is None:
+            out = [torch.empty(x.shape, dtype=torch.float32, pin_memory=True) if owner[i] == rank else None
+                   for i, x in enumerate(Xs)]
+        mine = [i for i in range(len(Xs)) if owner[i] == rank]
+        _run_host([Xs[i].contiguous() for i in mine], [out[i] for i in mine], torch.cuda.current_device(), chunks)
+        return [out[i] if owner[i] == rank else None for i in range(len(Xs))]
     stacked = torch.is_tensor(Xs)
     if stacked:
         if Xs.dim() != 3:

@@ -253,6 +253,228 @@ __global__ void __launch_bounds__(256) k_chol(float* __restrict__ A_all, float* 
     }
 }
 
+// ---- n <= 256: one CTA per matrix, the whole lower triangle in shared memory ----
+// The same operations in the same order as above (and as chol.cu), scheduled for one CTA of 16 warps: per step j the
+// panel tiles P_i = A[i, j] Linv[j]^T are computed in parallel and written in place (they are L[i, j]); then warp 0
+// updates the next diagonal tile A[j+1, j+1] -= P_{j+1} P_{j+1}^T and factors it (look-ahead), while warps 1-15 apply
+// A[i, k] -= P_i P_k^T to the other trailing tiles.  No global memory between the load and the stores of L and Li.
+constexpr int SM_NB = 8;                       // up to 8 x 8 tiles (n <= 256)
+constexpr int SM_TILE = TB * LDS;              // floats per stored tile
+constexpr int SM_NT = 512;
+
+__device__ __forceinline__ int lt_index(int ib, int kb) { return ib * (ib + 1) / 2 + kb; }
+
+// factor the tile T in place with one warp (lane = row), T <- L tile (zeros above the diagonal); inv <- its inverse;
+// rd <- the pivots' reciprocal square roots (chol.cu:115-180, as factor_diag)
+__device__ void factor_warp(float (*T)[LDS], float (*inv)[LDS], float* rd, float tau) {
+    const int i = threadIdx.x & 31;
+    float a[TB];
+#pragma unroll
+    for (int k = 0; k < TB; ++k) a[k] = T[i][k];
+    float myrd = 0.0f;
+#pragma unroll
+    for (int c = 0; c < TB; ++c) {
+        const float piv = fmaxf(__shfl_sync(0xffffffffu, a[c], c), tau);
+        const float r = det_rsqrt(piv);
+        const float l = (i > c) ? __fmul_rn(a[c], r) : ((i == c) ? __fmul_rn(piv, r) : 0.0f);
+        myrd = (i == c) ? r : myrd;
+        a[c] = l;
+#pragma unroll
+        for (int k = c + 1; k < TB; ++k) {
+            const float lk = __shfl_sync(0xffffffffu, l, k);
+            a[k] = __fmaf_rn(-((i >= k) ? l : 0.0f), lk, a[k]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < TB; ++k) T[i][k] = (k <= i) ? a[k] : 0.0f;
+    rd[i] = myrd;
+    __syncwarp();
+    const int kk = i;   // lane kk: column kk of the inverse by forward substitution
+    float x[TB];
+#pragma unroll
+    for (int r = 0; r < TB; ++r) {
+        float acc0 = (r == kk) ? 1.0f : 0.0f, acc1 = 0.0f, acc2 = 0.0f, acc3 = 0.0f;
+#pragma unroll
+        for (int m = 0; m + 3 < r; m += 4) {
+            acc0 = __fmaf_rn(-T[r][m], x[m], acc0);
+            acc1 = __fmaf_rn(-T[r][m + 1], x[m + 1], acc1);
+            acc2 = __fmaf_rn(-T[r][m + 2], x[m + 2], acc2);
+            acc3 = __fmaf_rn(-T[r][m + 3], x[m + 3], acc3);
+        }
+#pragma unroll
+        for (int m = (r / 4) * 4; m < r; ++m) acc0 = __fmaf_rn(-T[r][m], x[m], acc0);
+        x[r] = (r < kk) ? 0.0f : __fmul_rn(__fadd_rn(__fadd_rn(acc0, acc1), __fadd_rn(acc2, acc3)), rd[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < TB; ++r) inv[r][kk] = x[r];
+    __syncwarp();
+}
+
+// acc[u][v] = sum_m X[r0+u][m] Y[c0+v][m], an FMA chain from zero, m in order (chol.cu:63-71)
+__device__ __forceinline__ void mm22_at(const float (*X)[LDS], const float (*Y)[LDS], int r0, int c0, float acc[2][2]) {
+    acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.0f;
+#pragma unroll 8
+    for (int m = 0; m < TB; ++m) {
+        const float x0 = X[r0][m], x1 = X[r0 + 1][m], y0 = Y[c0][m], y1 = Y[c0 + 1][m];
+        acc[0][0] = __fmaf_rn(x0, y0, acc[0][0]);
+        acc[0][1] = __fmaf_rn(x0, y1, acc[0][1]);
+        acc[1][0] = __fmaf_rn(x1, y0, acc[1][0]);
+        acc[1][1] = __fmaf_rn(x1, y1, acc[1][1]);
+    }
+}
+
+__global__ void __launch_bounds__(SM_NT, 1) k_chol_smem(float* __restrict__ A_all, float* __restrict__ L_all,
+                                                        float* __restrict__ Li_all, int n,
+                                                        const double* __restrict__ rowsq, const float* __restrict__ tau_ptr,
+                                                        PassScal* __restrict__ scal, int zero_upper) {
+    extern __shared__ float sm_f[];
+    float (*tiles)[TB][LDS] = reinterpret_cast<float (*)[TB][LDS]>(sm_f);
+    const int nb = n / TB;
+    float (*inv)[LDS] = reinterpret_cast<float (*)[LDS]>(sm_f + (size_t)lt_index(nb, 0) * SM_TILE);
+    float* rd = sm_f + (size_t)(lt_index(nb, 0) + 1) * SM_TILE;
+    float* misc = rd + TB;   // [0] tau, [1] shift
+    const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5;
+    const float* A = A_all + (size_t)b * n * n;
+    float* L = L_all + (size_t)b * n * n;
+    float* Li = Li_all + (size_t)b * n * TB;
+
+    // the row sums of G^2 staged in shared memory (the inverse's space, free until the first factor), so that the
+    // in-order fp64 sum below does not wait on one global load per term
+    double* rs = reinterpret_cast<double*>(inv);
+    if (rowsq && tid < n) rs[tid] = rowsq[(size_t)b * n + tid];
+    // the lower tiles of A (row-major, float4 reads in batches of 6 per thread), upper tiles of L zeroed on request
+    const int n4 = n / 4, total = n * n4;
+    for (int e0 = tid; e0 < total; e0 += 6 * SM_NT) {
+        float4 v[6];
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            const int e = e0 + q * SM_NT;
+            if (e < total) {
+                const int r = e / n4, c = 4 * (e % n4);
+                if (c / TB <= r / TB) v[q] = __ldcg(reinterpret_cast<const float4*>(A + (size_t)r * n + c));
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            const int e = e0 + q * SM_NT;
+            if (e < total) {
+                const int r = e / n4, c = 4 * (e % n4);
+                const int ib = r / TB, kb = c / TB;
+                if (kb > ib) {
+                    if (zero_upper) *reinterpret_cast<float4*>(L + (size_t)r * n + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else {
+                    float* t = &tiles[lt_index(ib, kb)][r % TB][c % TB];
+                    t[0] = v[q].x; t[1] = v[q].y; t[2] = v[q].z; t[3] = v[q].w;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        if (rowsq) {
+            double tot = 0.0;
+            for (int a = 0; a < n; ++a) tot = __dadd_rn(tot, rs[a]);
+            const float nrm = __double2float_rn(__dsqrt_rn(tot));
+            misc[1] = __fmul_rn(1e-7f, nrm);
+            misc[0] = __fadd_rn(__fmul_rn(1e-8f, nrm), 1e-30f);
+            if (scal) {
+                scal[b].nrm = nrm;
+                scal[b].shift = misc[1];
+                scal[b].tau = misc[0];
+            }
+        } else {
+            misc[1] = 0.0f;
+            misc[0] = *tau_ptr;
+        }
+    }
+    __syncthreads();
+    const float tau = misc[0];
+    if (rowsq && tid < n) {   // G_ii += 1e-7 ||G||_F (kcholqr.py:108)
+        float* d = &tiles[lt_index(tid / TB, tid / TB)][tid % TB][tid % TB];
+        *d = __fadd_rn(*d, misc[1]);
+    }
+    __syncthreads();
+    if (warp == 0) factor_warp(tiles[lt_index(0, 0)], inv, rd, tau);
+    __syncthreads();
+
+    for (int jb = 0; jb < nb; ++jb) {
+        // the diagonal tile jb and its inverse are final: store them
+        for (int e = tid; e < TB * TB; e += SM_NT) {
+            const int r = e / TB, c = e % TB;
+            L[(size_t)(jb * TB + r) * n + jb * TB + c] = tiles[lt_index(jb, jb)][r][c];
+            Li[(size_t)(jb * TB + r) * TB + c] = inv[r][c];
+        }
+        if (jb + 1 == nb) break;
+        // panels P_i = A[i, jb] Linv^T, i > jb: all computed, then written in place (they are L[i, jb])
+        const int np = nb - 1 - jb;
+        float pv[4][2][2];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int t = tid + q * SM_NT;
+            if (t < np * 256) {
+                const int ib = jb + 1 + t / 256, w = t % 256;
+                mm22_at(tiles[lt_index(ib, jb)], inv, 2 * (w / 16), 2 * (w % 16), pv[q]);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int t = tid + q * SM_NT;
+            if (t < np * 256) {
+                const int ib = jb + 1 + t / 256, w = t % 256, r0 = 2 * (w / 16), c0 = 2 * (w % 16);
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int v = 0; v < 2; ++v) {
+                        tiles[lt_index(ib, jb)][r0 + u][c0 + v] = pv[q][u][v];
+                        L[(size_t)(ib * TB + r0 + u) * n + jb * TB + c0 + v] = pv[q][u][v];
+                    }
+            }
+        }
+        __syncthreads();
+        const int j1 = jb + 1;
+        if (warp == 0) {
+            // look-ahead: A[j1, j1] -= P_j1 P_j1^T, then factor it (inv <- Linv[j1])
+            float (*T)[LDS] = tiles[lt_index(j1, j1)];
+            const float (*P)[LDS] = tiles[lt_index(j1, jb)];
+            const int lane = tid & 31;
+            for (int w = lane; w < 256; w += 32) {
+                const int r0 = 2 * (w / 16), c0 = 2 * (w % 16);
+                float acc[2][2];
+                mm22_at(P, P, r0, c0, acc);
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int v = 0; v < 2; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
+            }
+            __syncwarp();
+            factor_warp(T, inv, rd, tau);
+        } else {
+            // A[i, k] -= P_i P_k^T for j1 <= k <= i, except (j1, j1)
+            const int ntr = np * (np + 1) / 2 - 1;
+            for (int t = tid - 32; t < ntr * 256; t += SM_NT - 32) {
+                int x = t / 256 + 1;   // trailing tile index, skipping (j1, j1) = index 0
+                int ii = 0;
+                while (x > ii) {
+                    x -= ii + 1;
+                    ++ii;
+                }
+                const int ib = j1 + ii, kb = j1 + x, w = t % 256, r0 = 2 * (w / 16), c0 = 2 * (w % 16);
+                float acc[2][2];
+                mm22_at(tiles[lt_index(ib, jb)], tiles[lt_index(kb, jb)], r0, c0, acc);
+                float (*T)[LDS] = tiles[lt_index(ib, kb)];
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int v = 0; v < 2; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+size_t chol_smem_bytes(int n) { return ((size_t)(n / TB) * (n / TB + 1) / 2 + 1) * SM_TILE * 4 + (TB + 2) * 4; }
+
 template <int C>
 static cudaError_t launch_chol_c(float* A, float* L, float* Li, int n, int B, const double* rowsq,
                                  const float* tau_ptr, PassScal* scal, int zero_upper, cudaStream_t st) {
@@ -279,6 +501,13 @@ static cudaError_t launch_chol_c(float* A, float* L, float* Li, int n, int B, co
 cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, const float* tau_ptr,
                         PassScal* scal, int zero_upper, cudaStream_t st) {
     const int nb = n / TB;
+    if (nb <= SM_NB) {   // the whole lower triangle fits in one CTA's shared memory
+        const size_t smem = chol_smem_bytes(n);
+        cudaError_t e = cudaFuncSetAttribute(k_chol_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k_chol_smem<<<B, SM_NT, smem, st>>>(A, L, Li, n, rowsq, tau_ptr, scal, zero_upper);
+        return cudaGetLastError();
+    }
     int C = (B >= 32) ? 2 : 8;
     if (nb <= 2) C = 1;
     else if (nb <= 4 && C > 2) C = 2;

@@ -42,6 +42,22 @@ def test_batched_equals_single_bitwise():
         assert all(_bits(a, b) for a, b in zip(got, single))
 
 
+def test_host_inputs_pipelined_match_device_bitwise():
+    """CPU inputs: copies in, kernels and copies out overlapped chunk by chunk; same bits as the device path"""
+    Xs = [cases.cfg3_matrix(i, K=1024).pin_memory() for i in range(11)]
+    Xs.append(cases.make_case(768, 512, "mixed_c6").pin_memory())
+    want = [orth(x.cuda()).cpu() for x in Xs]
+    out = [torch.full(x.shape, float("nan")).pin_memory() for x in Xs]
+    for chunks in (1, 3, 8):
+        got = orth_batched(Xs, out=out, chunks=chunks)
+        torch.cuda.synchronize()
+        assert all(g is o for g, o in zip(got, out))
+        assert all(not g.is_cuda and _bits(g, w) for g, w in zip(got, want)), chunks
+    got = orth_batched([x.clone() for x in Xs])   # unpinned inputs, outputs allocated by the call
+    torch.cuda.synchronize()
+    assert all(_bits(g, w) for g, w in zip(got, want))
+
+
 def test_batched_mixed_shapes():
     Xs = [cases.cfg4_matrix(i, n_small=3, K_small=1024, K_big=2048, N=512).cuda() for i in range(5)]
     Xs.append(cases.make_case(768, 512, "mixed_c6").cuda())

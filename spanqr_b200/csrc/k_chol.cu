@@ -258,6 +258,9 @@ __global__ void __launch_bounds__(256) k_chol(float* __restrict__ A_all, float* 
 // panel tiles P_i = A[i, j] Linv[j]^T are computed in parallel and written in place (they are L[i, j]); then warp 0
 // updates the next diagonal tile A[j+1, j+1] -= P_{j+1} P_{j+1}^T and factors it (look-ahead), while warps 1-15 apply
 // A[i, k] -= P_i P_k^T to the other trailing tiles.  No global memory between the load and the stores of L and Li.
+__device__ __forceinline__ void tc_named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 constexpr int SM_NB = 8;                       // up to 8 x 8 tiles (n <= 256)
 constexpr int SM_TILE = TB * LDS;              // floats per stored tile
 constexpr int SM_NT = 512;
@@ -265,7 +268,7 @@ constexpr int SM_NT = 512;
 __device__ __forceinline__ int lt_index(int ib, int kb) { return ib * (ib + 1) / 2 + kb; }
 
 // factor the tile T in place with one warp (lane = row), T <- L tile (zeros above the diagonal); inv <- its inverse;
-// rd <- the pivots' reciprocal square roots (chol.cu:115-180, as factor_diag)
+// rd <- the pivots' reciprocal square roots (chol.cu:115-180, the operations of factor_diag)
 __device__ void factor_warp(float (*T)[LDS], float (*inv)[LDS], float* rd, float tau) {
     const int i = threadIdx.x & 31;
     float a[TB];
@@ -310,16 +313,23 @@ __device__ void factor_warp(float (*T)[LDS], float (*inv)[LDS], float* rd, float
     __syncwarp();
 }
 
-// acc[u][v] = sum_m X[r0+u][m] Y[c0+v][m], an FMA chain from zero, m in order (chol.cu:63-71)
-__device__ __forceinline__ void mm22_at(const float (*X)[LDS], const float (*Y)[LDS], int r0, int c0, float acc[2][2]) {
-    acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.0f;
-#pragma unroll 8
+// acc[u][v] = sum_m X[r0+u][m] Y[c0+v][m] for a 4 x 4 block, FMA chains from zero, m in order (chol.cu:63-71)
+__device__ __forceinline__ void mm44_at(const float (*X)[LDS], const float (*Y)[LDS], int r0, int c0, float acc[4][4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[u][v] = 0.0f;
+#pragma unroll 4
     for (int m = 0; m < TB; ++m) {
-        const float x0 = X[r0][m], x1 = X[r0 + 1][m], y0 = Y[c0][m], y1 = Y[c0 + 1][m];
-        acc[0][0] = __fmaf_rn(x0, y0, acc[0][0]);
-        acc[0][1] = __fmaf_rn(x0, y1, acc[0][1]);
-        acc[1][0] = __fmaf_rn(x1, y0, acc[1][0]);
-        acc[1][1] = __fmaf_rn(x1, y1, acc[1][1]);
+        float x[4], y[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = X[r0 + u][m];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) y[v] = Y[c0 + v][m];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int v = 0; v < 4; ++v) acc[u][v] = __fmaf_rn(x[u], y[v], acc[u][v]);
     }
 }
 
@@ -405,68 +415,59 @@ __global__ void __launch_bounds__(SM_NT, 1) k_chol_smem(float* __restrict__ A_al
             Li[(size_t)(jb * TB + r) * TB + c] = inv[r][c];
         }
         if (jb + 1 == nb) break;
-        // panels P_i = A[i, jb] Linv^T, i > jb: all computed, then written in place (they are L[i, jb])
+        // panels P_i = A[i, jb] Linv^T, i > jb (64 blocks of 4 x 4 per tile): all computed, then written in place
+        // (they are L[i, jb])
         const int np = nb - 1 - jb;
-        float pv[4][2][2];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int t = tid + q * SM_NT;
-            if (t < np * 256) {
-                const int ib = jb + 1 + t / 256, w = t % 256;
-                mm22_at(tiles[lt_index(ib, jb)], inv, 2 * (w / 16), 2 * (w % 16), pv[q]);
-            }
-        }
+        float pv[4][4];
+        const int ptask = tid, pib = jb + 1 + ptask / 64, pw = ptask % 64;
+        const bool has_p = ptask < np * 64;
+        if (has_p) mm44_at(tiles[lt_index(pib, jb)], inv, 4 * (pw / 8), 4 * (pw % 8), pv);
         __syncthreads();
+        if (has_p) {
+            const int r0 = 4 * (pw / 8), c0 = 4 * (pw % 8);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int t = tid + q * SM_NT;
-            if (t < np * 256) {
-                const int ib = jb + 1 + t / 256, w = t % 256, r0 = 2 * (w / 16), c0 = 2 * (w % 16);
+            for (int u = 0; u < 4; ++u) {
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
-#pragma unroll
-                    for (int v = 0; v < 2; ++v) {
-                        tiles[lt_index(ib, jb)][r0 + u][c0 + v] = pv[q][u][v];
-                        L[(size_t)(ib * TB + r0 + u) * n + jb * TB + c0 + v] = pv[q][u][v];
-                    }
+                for (int v = 0; v < 4; ++v) tiles[lt_index(pib, jb)][r0 + u][c0 + v] = pv[u][v];
+                *reinterpret_cast<float4*>(L + (size_t)(pib * TB + r0 + u) * n + jb * TB + c0) =
+                    make_float4(pv[u][0], pv[u][1], pv[u][2], pv[u][3]);
             }
         }
         __syncthreads();
         const int j1 = jb + 1;
-        if (warp == 0) {
-            // look-ahead: A[j1, j1] -= P_j1 P_j1^T, then factor it (inv <- Linv[j1])
+        if (warp < 4) {
+            // look-ahead on warps 0-3: A[j1, j1] -= P_j1 P_j1^T (64 blocks of 4 x 4), then warp 0 factors it
             float (*T)[LDS] = tiles[lt_index(j1, j1)];
             const float (*P)[LDS] = tiles[lt_index(j1, jb)];
-            const int lane = tid & 31;
-            for (int w = lane; w < 256; w += 32) {
-                const int r0 = 2 * (w / 16), c0 = 2 * (w % 16);
-                float acc[2][2];
-                mm22_at(P, P, r0, c0, acc);
+            for (int w = tid; w < 64; w += 128) {
+                const int r0 = 4 * (w / 8), c0 = 4 * (w % 8);
+                float acc[4][4];
+                mm44_at(P, P, r0, c0, acc);
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
+                for (int u = 0; u < 4; ++u)
 #pragma unroll
-                    for (int v = 0; v < 2; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
+                    for (int v = 0; v < 4; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
             }
-            __syncwarp();
-            factor_warp(T, inv, rd, tau);
+            tc_named_sync(1, 128);
+            if (warp == 0) factor_warp(T, inv, rd, tau);
         } else {
-            // A[i, k] -= P_i P_k^T for j1 <= k <= i, except (j1, j1)
+            // A[i, k] -= P_i P_k^T for j1 <= k <= i, except (j1, j1), on warps 4-15
             const int ntr = np * (np + 1) / 2 - 1;
-            for (int t = tid - 32; t < ntr * 256; t += SM_NT - 32) {
-                int x = t / 256 + 1;   // trailing tile index, skipping (j1, j1) = index 0
+            for (int t = tid - 128; t < ntr * 64; t += SM_NT - 128) {
+                int x = t / 64 + 1;   // trailing tile index, skipping (j1, j1) = index 0
                 int ii = 0;
                 while (x > ii) {
                     x -= ii + 1;
                     ++ii;
                 }
-                const int ib = j1 + ii, kb = j1 + x, w = t % 256, r0 = 2 * (w / 16), c0 = 2 * (w % 16);
-                float acc[2][2];
-                mm22_at(tiles[lt_index(ib, jb)], tiles[lt_index(kb, jb)], r0, c0, acc);
+                const int ib = j1 + ii, kb = j1 + x, w = t % 64, r0 = 4 * (w / 8), c0 = 4 * (w % 8);
+                float acc[4][4];
+                mm44_at(tiles[lt_index(ib, jb)], tiles[lt_index(kb, jb)], r0, c0, acc);
                 float (*T)[LDS] = tiles[lt_index(ib, kb)];
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
+                for (int u = 0; u < 4; ++u)
 #pragma unroll
-                    for (int v = 0; v < 2; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
+                    for (int v = 0; v < 4; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
             }
         }
         __syncthreads();

@@ -7,6 +7,7 @@ Every call runs on libspanqr's CUDA kernels on the current stream, with no host 
 fallback: an unsupported shape raises (the reference silently falls back to torch.linalg.qr for r % 32 != 0,
 kcholqr.py:98-99, and routes r > 512 to block Gram-Schmidt, orth.py:18-19).
 """
+import os
 import threading
 
 import torch
@@ -19,7 +20,11 @@ DUST_SEED = 20261018  # candidates/kcholqr.py:86
 
 _Z = {}
 _WS = {}
-_lock = threading.Lock()
+_GRAPHS = {}
+_lock = threading.RLock()
+# orth() replays one CUDA graph per (device, stream, shape): the ~30 launches of a call go to the GPU as one unit
+# (SPANQR_GRAPHS=0 launches them one by one instead)
+USE_GRAPHS = os.environ.get("SPANQR_GRAPHS", "1") != "0"
 
 
 def zdust(K, r, device):
@@ -79,9 +84,46 @@ def orth(X: torch.Tensor) -> torch.Tensor:
     dev = X.device
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev)
-        Z = zdust(K, r, dev)
+        if USE_GRAPHS:
+            g = _graph(dev, stream, K, r)
+            g.x.copy_(X)
+            g.graph.replay()
+            return g.q.clone()
         Q = torch.empty((K, r), dtype=torch.float32, device=dev)
-        ws = workspace(dev, K, r, 1, stream)
-        _lib.check(_lib.lib().spanqr_orth_f32(X.data_ptr(), r, Q.data_ptr(), r, K, r, Z.data_ptr(), ws.data_ptr(),
-                                              ws.numel(), stream.cuda_stream), f"orth({K}x{r})")
+        _call(X, Q, zdust(K, r, dev), workspace(dev, K, r, 1, stream), stream.cuda_stream)
     return Q
+
+
+def _call(X, Q, Z, ws, stream_handle):
+    K, r = X.shape
+    _lib.check(_lib.lib().spanqr_orth_f32(X.data_ptr(), r, Q.data_ptr(), r, K, r, Z.data_ptr(), ws.data_ptr(),
+                                          ws.numel(), stream_handle), f"orth({K}x{r})")
+
+
+class _Graph:
+    """one captured orth(K x r) with its own input, output and workspace (graphs bake in their pointers)"""
+
+    def __init__(self, dev, stream, K, r, Z):
+        self.x = torch.zeros((K, r), dtype=torch.float32, device=dev)
+        self.q = torch.empty_like(self.x)
+        self.ws = torch.empty(_lib.workspace_bytes(K, r, 1), dtype=torch.uint8, device=dev)
+        self.z = Z
+        _call(self.x, self.q, self.z, self.ws, stream.cuda_stream)   # first run eagerly: kernels loaded, attributes set
+        self.graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        with torch.cuda.graph(self.graph, stream=cap):
+            _call(self.x, self.q, self.z, self.ws, cap.cuda_stream)
+        stream.wait_stream(cap)
+
+
+def _graph(dev, stream, K, r):
+    key = (str(dev), stream.cuda_stream, K, r)
+    g = _GRAPHS.get(key)
+    if g is None:
+        Z = zdust(K, r, dev)   # outside the lock: zdust takes it too
+        with _lock:
+            g = _GRAPHS.get(key)
+            if g is None:
+                g = _GRAPHS[key] = _Graph(dev, stream, K, r, Z)
+    return g

@@ -117,3 +117,21 @@ def test_rejects_unsupported_shapes_loudly():
         orth(torch.zeros(100, 48, device="cuda"))
     with pytest.raises(TypeError):
         orth(torch.zeros(100, 64, device="cuda", dtype=torch.float64))
+
+
+def test_graph_replay_equals_eager_launches():
+    """orth() replays one captured CUDA graph per shape; the bits equal the launch-by-launch path, call after call"""
+    from spanqr_b200 import core
+    for K, r, name in [(3584, 256, "mixed_c2"), (768, 512, "ttf_cu4_t1e-2"), (1000, 96, "mixed_c4")]:
+        X = cases.make_case(K, r, name).cuda() if (K, r) in cases.SHAPES else torch.randn(K, r, device="cuda")
+        saved = core.USE_GRAPHS
+        try:
+            core.USE_GRAPHS = False
+            want = orth(X)
+            core.USE_GRAPHS = True
+            got = [orth(X) for _ in range(3)]
+        finally:
+            core.USE_GRAPHS = saved
+        torch.cuda.synchronize()
+        for g in got:
+            assert gu.bits_equal(g.cpu().numpy(), want.cpu().numpy()), (K, r)

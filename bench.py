@@ -175,7 +175,7 @@ def alg_bytes_per_matrix(kind, K, r):
     averaged over that kind's launches in one orth (k_trsm: pass 1 reads X and Z, passes 2-3 read Y; all write Y)"""
     kr4 = 4.0 * K * r
     return {"k_absmax": kr4, "k_gram_tc": kr4, "k_gram_tc_acc": kr4, "k_trsm": (3 + 2 + 2) * kr4 / 3.0,
-            "k_ns_update": 2 * kr4, "k_gram_reduce": 4.0 * r * r, "k_rowsq": 4.0 * r * r,
+            "k_ns_update": 2 * kr4, "k_gram_reduce": 4.0 * r * r,
             "k_chol": 3 * 4.0 * r * r, "k_trsm_w": 4.0 * r * r, "k_setup": 16.0}.get(kind, 0.0)
 
 

@@ -28,8 +28,8 @@ int cuda_fail(cudaError_t e) {
 }
 
 // ---- optional per-kernel timing (spanqr_timing_*) ----
-enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_ROWSQ, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_GRAM_ACC, K_COUNT };
-const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce", "k_rowsq",
+enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_GRAM_ACC, K_COUNT };
+const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce",
                                          "k_chol", "k_trsm_w", "k_trsm", "k_ns_update", "k_gram_tc_acc"};
 struct TimedLaunch {
     int kind;
@@ -140,10 +140,9 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
                             : launch_gram_tc(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, 0, P, status,
                                              st);
         }));
-        SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 0, G, st); }));
-        SPQ_TRY(timed(K_ROWSQ, st, [&] { return launch_rowsq(G, r, B, rowsq, st); }));
+        SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 0, G, rowsq, st); }));
         SPQ_TRY(timed(K_CHOL, st, [&] {
-            return launch_chol(G, Lm, Li, r, B, rowsq, nullptr, scal + (size_t)pass * B, 0, st);
+            return launch_chol(G, Lm, Li, r, B, rowsq, gram_sq_parts(gp), nullptr, scal + (size_t)pass * B, 0, st);
         }));
         if (r <= 256) SPQ_TRY(timed(K_TRSM_W, st, [&] { return launch_trsm_w(Lm, Li, r, B, W, st); }));
         SPQ_TRY(timed(K_TRSM, st, [&] {
@@ -163,7 +162,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
                        : launch_gram_tc(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, last ? 1 : 0, P, status,
                                         st);
         }));
-        SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, st); }));
+        SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, nullptr, st); }));
         // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel
         SPQ_TRY(timed(K_NS, st, [&] {
             return r <= 256 ? launch_ns_ws(p, K, r, ldq, B, G, maps, reinterpret_cast<char*>(P), status, st)
@@ -316,7 +315,7 @@ int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_
     if (e == cudaSuccess)
         e = launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, 1, at<float>(ws, l.P),
                            at<int>(ws, l.status), st);
-    if (e == cudaSuccess) e = launch_gram_reduce(at<float>(ws, l.P), n, 1, gp, 0, G, st);
+    if (e == cudaSuccess) e = launch_gram_reduce(at<float>(ws, l.P), n, 1, gp, 0, G, nullptr, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 
@@ -330,7 +329,7 @@ int spanqr_chol_f32(const float* G, int n, const float* d_tau, float* L, float* 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     float* A = at<float>(ws, l.G);
     cudaError_t e = cudaMemcpyAsync(A, G, sizeof(float) * (size_t)n * n, cudaMemcpyDeviceToDevice, st);
-    if (e == cudaSuccess) e = launch_chol(A, L, Li, n, 1, nullptr, d_tau, nullptr, 1, st);
+    if (e == cudaSuccess) e = launch_chol(A, L, Li, n, 1, nullptr, 0, d_tau, nullptr, 1, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 

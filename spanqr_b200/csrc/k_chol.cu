@@ -136,7 +136,7 @@ __device__ __forceinline__ void sync_matrix() {
 template <int C>
 __global__ void __launch_bounds__(256) k_chol(float* __restrict__ A_all, float* __restrict__ L_all,
                                               float* __restrict__ Li_all, int n, const double* __restrict__ rowsq,
-                                              const float* __restrict__ tau_ptr, PassScal* __restrict__ scal,
+                                              int nsq, const float* __restrict__ tau_ptr, PassScal* __restrict__ scal,
                                               int zero_upper) {
     __shared__ CholSmem S;
     __shared__ float s_tau, s_shift;
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(256) k_chol(float* __restrict__ A_all, float* 
     if (threadIdx.x == 0) {
         if (rowsq) {
             double tot = 0.0;
-            for (int a = 0; a < n; ++a) tot = __dadd_rn(tot, rowsq[(size_t)b * n + a]);
+            for (int a = 0; a < nsq; ++a) tot = __dadd_rn(tot, rowsq[(size_t)b * n + a]);
             const float nrm = __double2float_rn(__dsqrt_rn(tot));
             s_shift = __fmul_rn(1e-7f, nrm);
             s_tau = __fadd_rn(__fmul_rn(1e-8f, nrm), 1e-30f);
@@ -335,8 +335,9 @@ __device__ __forceinline__ void mm44_at(const float (*X)[LDS], const float (*Y)[
 
 __global__ void __launch_bounds__(SM_NT, 1) k_chol_smem(float* __restrict__ A_all, float* __restrict__ L_all,
                                                         float* __restrict__ Li_all, int n,
-                                                        const double* __restrict__ rowsq, const float* __restrict__ tau_ptr,
-                                                        PassScal* __restrict__ scal, int zero_upper) {
+                                                        const double* __restrict__ rowsq, int nsq,
+                                                        const float* __restrict__ tau_ptr, PassScal* __restrict__ scal,
+                                                        int zero_upper) {
     extern __shared__ float sm_f[];
     float (*tiles)[TB][LDS] = reinterpret_cast<float (*)[TB][LDS]>(sm_f);
     const int nb = n / TB;
@@ -351,7 +352,7 @@ __global__ void __launch_bounds__(SM_NT, 1) k_chol_smem(float* __restrict__ A_al
     // the row sums of G^2 staged in shared memory (the inverse's space, free until the first factor), so that the
     // in-order fp64 sum below does not wait on one global load per term
     double* rs = reinterpret_cast<double*>(inv);
-    if (rowsq && tid < n) rs[tid] = rowsq[(size_t)b * n + tid];
+    if (rowsq && tid < nsq) rs[tid] = rowsq[(size_t)b * n + tid];
     // the lower tiles of A (row-major, float4 reads in batches of 6 per thread), upper tiles of L zeroed on request
     const int n4 = n / 4, total = n * n4;
     for (int e0 = tid; e0 < total; e0 += 6 * SM_NT) {
@@ -383,7 +384,7 @@ __global__ void __launch_bounds__(SM_NT, 1) k_chol_smem(float* __restrict__ A_al
     if (tid == 0) {
         if (rowsq) {
             double tot = 0.0;
-            for (int a = 0; a < n; ++a) tot = __dadd_rn(tot, rs[a]);
+            for (int a = 0; a < nsq; ++a) tot = __dadd_rn(tot, rs[a]);
             const float nrm = __double2float_rn(__dsqrt_rn(tot));
             misc[1] = __fmul_rn(1e-7f, nrm);
             misc[0] = __fadd_rn(__fmul_rn(1e-8f, nrm), 1e-30f);
@@ -477,7 +478,7 @@ __global__ void __launch_bounds__(SM_NT, 1) k_chol_smem(float* __restrict__ A_al
 size_t chol_smem_bytes(int n) { return ((size_t)(n / TB) * (n / TB + 1) / 2 + 1) * SM_TILE * 4 + (TB + 2) * 4; }
 
 template <int C>
-static cudaError_t launch_chol_c(float* A, float* L, float* Li, int n, int B, const double* rowsq,
+static cudaError_t launch_chol_c(float* A, float* L, float* Li, int n, int B, const double* rowsq, int nsq,
                                  const float* tau_ptr, PassScal* scal, int zero_upper, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(C * B);
@@ -495,18 +496,18 @@ static cudaError_t launch_chol_c(float* A, float* L, float* Li, int n, int B, co
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, k_chol<C>, A, L, Li, n, rowsq, tau_ptr, scal, zero_upper);
+    return cudaLaunchKernelEx(&cfg, k_chol<C>, A, L, Li, n, rowsq, nsq, tau_ptr, scal, zero_upper);
 }
 
 // Cluster size: a lone matrix spreads its trailing updates over 8 SMs; batches use 2 (many clusters at once).
-cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, const float* tau_ptr,
-                        PassScal* scal, int zero_upper, cudaStream_t st) {
+cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, int nsq,
+                        const float* tau_ptr, PassScal* scal, int zero_upper, cudaStream_t st) {
     const int nb = n / TB;
     if (nb <= SM_NB) {   // the whole lower triangle fits in one CTA's shared memory
         const size_t smem = chol_smem_bytes(n);
         cudaError_t e = cudaFuncSetAttribute(k_chol_smem, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        k_chol_smem<<<B, SM_NT, smem, st>>>(A, L, Li, n, rowsq, tau_ptr, scal, zero_upper);
+        k_chol_smem<<<B, SM_NT, smem, st>>>(A, L, Li, n, rowsq, nsq, tau_ptr, scal, zero_upper);
         return cudaGetLastError();
     }
     int C = (B >= 32) ? 2 : 8;
@@ -514,9 +515,9 @@ cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const doubl
     else if (nb <= 4 && C > 2) C = 2;
     cudaError_t e;
     switch (C) {
-        case 1: e = launch_chol_c<1>(A, L, Li, n, B, rowsq, tau_ptr, scal, zero_upper, st); break;
-        case 2: e = launch_chol_c<2>(A, L, Li, n, B, rowsq, tau_ptr, scal, zero_upper, st); break;
-        default: e = launch_chol_c<8>(A, L, Li, n, B, rowsq, tau_ptr, scal, zero_upper, st); break;
+        case 1: e = launch_chol_c<1>(A, L, Li, n, B, rowsq, nsq, tau_ptr, scal, zero_upper, st); break;
+        case 2: e = launch_chol_c<2>(A, L, Li, n, B, rowsq, nsq, tau_ptr, scal, zero_upper, st); break;
+        default: e = launch_chol_c<8>(A, L, Li, n, B, rowsq, nsq, tau_ptr, scal, zero_upper, st); break;
     }
     if (e != cudaSuccess) return e;
     return cudaGetLastError();

@@ -1,8 +1,10 @@
-// The Gram's fixed-order reduction over splits, and the row sums of squares of G.
+// The Gram's fixed-order reduction over splits.
 //
 // k_gram_reduce: G = fp64 sum of the split partials of k_gram_tc (128 x 128 tiles of the upper triangle) in split
 // order, rounded to fp32 and mirrored, as tri.py:375 sums its splits (P.sum(0, float64).float()); with make_D it
-// writes D = 0.5 (I - G) instead (kcholqr.py:21).
+// writes D = 0.5 (I - G) instead (kcholqr.py:21).  Without make_D it also writes, per strip, the fp64 sum of the
+// squares of the G entries it wrote (every entry of G is written exactly once): the Cholesky adds these partial sums
+// in a fixed order for ||G||_F (kcholqr.py:107).
 #include "kernels.h"
 
 namespace spq {
@@ -14,7 +16,7 @@ namespace spq {
 constexpr int RSTRIP = 32;
 
 __global__ void __launch_bounds__(256) k_gram_reduce(const float* __restrict__ P, int n, GramPlan gp, int make_D,
-                                                     float* __restrict__ G) {
+                                                     float* __restrict__ G, double* __restrict__ sq) {
     constexpr int T = GRAM_TILE;
     const int tile = blockIdx.x / (T / RSTRIP), r0 = (blockIdx.x % (T / RSTRIP)) * RSTRIP, b = blockIdx.y;
     int ti, tj;
@@ -43,45 +45,44 @@ __global__ void __launch_bounds__(256) k_gram_reduce(const float* __restrict__ P
         }
     }
     __syncthreads();
+    double q = 0.0;   // squares of the entries this thread writes
     // rows: G[a][c]; in a diagonal tile only c >= a
     for (int e = threadIdx.x; e < RSTRIP * T; e += blockDim.x) {
         const int r = e / T, c = e % T;
         const int a = ti * T + r0 + r, cg = tj * T + c;
         if (a >= n || cg >= n || (diag && cg < a)) continue;
-        G[(size_t)b * n * n + (size_t)a * n + cg] = S[r][c];
+        const float g = S[r][c];
+        G[(size_t)b * n * n + (size_t)a * n + cg] = g;
+        q = __fma_rn((double)g, (double)g, q);
     }
     // columns: G[c][a]; in a diagonal tile only c > a
     for (int e = threadIdx.x; e < RSTRIP * T; e += blockDim.x) {
         const int c = e / RSTRIP, r = e % RSTRIP;
         const int a = ti * T + r0 + r, cg = tj * T + c;
         if (a >= n || cg >= n || (diag && cg <= a)) continue;
-        G[(size_t)b * n * n + (size_t)cg * n + a] = S[r][c];
+        const float g = S[r][c];
+        G[(size_t)b * n * n + (size_t)cg * n + a] = g;
+        q = __fma_rn((double)g, (double)g, q);
+    }
+    if (sq) {   // fixed-order block sum: butterfly within each warp, then the warps in order
+        __shared__ double wsum[8];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) q = __dadd_rn(q, __shfl_xor_sync(0xffffffffu, q, o));
+        if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = q;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = wsum[0];
+            for (int w = 1; w < (int)(blockDim.x >> 5); ++w) t = __dadd_rn(t, wsum[w]);
+            sq[(size_t)b * n + blockIdx.x] = t;
+        }
     }
 }
 
-// rowsq[b][a] = sum over c of G[b][a][c]^2 in fp64, c in order; G is exactly symmetric, so column a is read
-// (coalesced) in place of row a.
-__global__ void __launch_bounds__(128) k_rowsq(const float* __restrict__ G, int n, double* __restrict__ rowsq) {
-    const int b = blockIdx.y;
-    const int a = blockIdx.x * blockDim.x + threadIdx.x;
-    if (a >= n) return;
-    const float* Gb = G + (size_t)b * n * n;
-    double row = 0.0;
-    for (int c = 0; c < n; ++c) {
-        const double g = (double)Gb[(size_t)c * n + a];
-        row = __dadd_rn(row, __dmul_rn(g, g));
-    }
-    rowsq[(size_t)b * n + a] = row;
-}
+int gram_sq_parts(const GramPlan& gp) { return gp.tiles * (GRAM_TILE / RSTRIP); }
 
-cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G,
+cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G, double* sq,
                                cudaStream_t st) {
-    k_gram_reduce<<<dim3(gp.tiles * (GRAM_TILE / RSTRIP), B), 256, 0, st>>>(P, n, gp, make_D, G);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_rowsq(const float* G, int n, int B, double* rowsq, cudaStream_t st) {
-    k_rowsq<<<dim3(cdiv(n, 128), B), 128, 0, st>>>(G, n, rowsq);
+    k_gram_reduce<<<dim3(gram_sq_parts(gp), B), 256, 0, st>>>(P, n, gp, make_D, G, make_D ? nullptr : sq);
     return cudaGetLastError();
 }
 

@@ -66,15 +66,16 @@ cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B,
 cudaError_t launch_gram_ws(PtrArg p, Src src, int K, int n, int B, const GramPlan& gp, const char* maps, ScaleArg sc,
                            float* P, int* status, cudaStream_t st);
 
-// G[b] (n x n, both triangles) = fp64 sum over splits; with make_D, D = 0.5 (I - G) instead
-cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G,
+// G[b] (n x n, both triangles) = fp64 sum over splits; with make_D, D = 0.5 (I - G) instead.  Without make_D (and sq
+// not null) also sq[b * n + i], i < gram_sq_parts(gp) (<= n): fp64 partial sums of the squares of G's entries
+int gram_sq_parts(const GramPlan& gp);
+cudaError_t launch_gram_reduce(const float* P, int n, int B, const GramPlan& gp, int make_D, float* G, double* sq,
                                cudaStream_t st);
-// rowsq[b][a] = sum_c G[b][a][c]^2 in fp64, columns in order
-cudaError_t launch_rowsq(const float* G, int n, int B, double* rowsq, cudaStream_t st);
 
-// Clamped Cholesky of A[b] (n x n, lower tiles read, overwritten).  Pipeline mode (rowsq != null): nrm from rowsq,
-// A_ii += 1e-7 nrm, tau = 1e-8 nrm + 1e-30, scalars to scal[b].  Component mode: tau = *tau_ptr, no shift.
-cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, const float* tau_ptr,
+// Clamped Cholesky of A[b] (n x n, lower tiles read, overwritten).  Pipeline mode (sq != null): nrm = sqrt of the sum
+// of sq[b * n + 0 .. nsq) in order, A_ii += 1e-7 nrm, tau = 1e-8 nrm + 1e-30, scalars to scal[b].  Component mode:
+// tau = *tau_ptr, no shift.
+cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* sq, int nsq, const float* tau_ptr,
                         PassScal* scal, int zero_upper, cudaStream_t st);
 
 // The solve's coefficient image W (W_jj = Li_j, W_jk = -Li_j L_jk, split tf32 tiles of 4 KB per part), grouped by

@@ -66,7 +66,7 @@ cudaError_t timed(int kind, cudaStream_t st, F&& launch) {
 size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Layout {
-    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, W, maps, P, total;
+    size_t status, ptrs, maxbits, scal, rowsq, G, L, Li, W, maps, nss, P, total;
 };
 
 Layout layout(int K, int r, int B) {
@@ -82,10 +82,11 @@ Layout layout(int K, int r, int B) {
     l.L = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
     l.W = o;       o += (r <= 256) ? al256(trsm_w_bytes(r) * (size_t)B) : 0;
-    l.maps = o;    o += (r <= 256) ? al256((size_t)TMAPS_PER_MATRIX * 128 * B) : 0;
+    l.maps = o;    o += al256((size_t)TMAPS_PER_MATRIX * 128 * B);
+    l.nss = o;     o += (r > 256) ? al256(sizeof(float) * (size_t)B * K * 256) : 0;   // polish update, first half
     // the Gram's split partials; the polish step's D image reuses them once they are reduced
     size_t pbytes = sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE;
-    if (r <= 256 && ns_dimg_bytes(r) * B > pbytes) pbytes = ns_dimg_bytes(r) * B;
+    if (ns_dimg_bytes(r) * B > pbytes) pbytes = ns_dimg_bytes(r) * B;
     l.P = o;       o += al256(pbytes);
     l.total = o;
     return l;
@@ -129,7 +130,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         if ((e = (call)) != cudaSuccess) return cuda_fail(e); \
     } while (0)
     SPQ_TRY(timed(K_ABSMAX, st, [&] { return launch_absmax(p, K, r, ldx, B, maxbits, st); }));
-    if (r <= 256) SPQ_TRY(timed(K_SETUP, st, [&] { return launch_tmaps(p, K, r, ldx, ldq, B, ws, maps, st); }));
+    SPQ_TRY(timed(K_SETUP, st, [&] { return launch_tmaps(p, K, r, ldx, ldq, B, ws, maps, st); }));
     for (int pass = 0; pass < PASSES; ++pass) {
         const bool first = pass == 0;
         const ScaleArg sc = first ? ScaleArg{maxbits, nullptr} : ScaleArg{nullptr, nullptr};
@@ -165,8 +166,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, nullptr, st); }));
         // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel
         SPQ_TRY(timed(K_NS, st, [&] {
-            return r <= 256 ? launch_ns_ws(p, K, r, ldq, B, G, maps, reinterpret_cast<char*>(P), status, st)
-                            : launch_ns_update(p, K, r, ldq, B, G, st);
+            return launch_ns_ws(p, K, r, ldq, B, G, maps, reinterpret_cast<char*>(P), at<float>(ws, l.nss), status, st);
         }));
     }
 #undef SPQ_TRY

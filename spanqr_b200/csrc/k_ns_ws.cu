@@ -4,9 +4,11 @@
 // k_d_image splits D (symmetric, from k_gram_reduce) once per matrix into tf32 hi/lo operand tiles laid out as the
 // update's shared-memory B operand: for each chunk of 32 contraction indices, rows c = 0..n-1 (row c of D is column
 // c) x 32 k, K-major with the 128-byte swizzle, hi part then lo part.  k_ns_ws then streams those chunks by bulk copy.
-// One CTA = 128 rows of one matrix, all n output columns; warp roles: 0-3 epilogue (TMEM lanes = rows: y + acc,
-// written in place), 4-7 convert (raw 32-column tile of Q by TMA -> tf32 hi | lo, K-major), 8 products (one
-// thread, fixed order), 9 copies (one thread).  Accuracy: |Q D| is about 1e-2 |Q| or less, so 3xTF32 and the
+// One CTA = 128 rows of one matrix, all n output columns, in nh = 1 (n <= 256) or 2 column halves of N = n / nh
+// (TMEM holds the large and small accumulators of at most 256 columns); warp roles: 0-3 epilogue (TMEM lanes = rows:
+// y + acc), 4-7 convert (raw 32-column tile of Q by TMA -> tf32 hi | lo, K-major), 8 products (one thread, fixed
+// order), 9 copies (one thread).  The last half is written in place; an earlier half still feeds the later halves'
+// products, so its new values wait in `scratch` and are copied in after the last half.  Accuracy: |Q D| is about 1e-2 |Q| or less, so 3xTF32 and the
 // truncating fp32 accumulation leave errors below one ulp of Q.
 #include "kernels.h"
 #include "tc.cuh"
@@ -27,9 +29,10 @@ constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TCOLS = 512;                 // large at 0, small at 256
 constexpr int ERR_TIMEOUT = 0x20;
 // mbarriers (x2 per stage): raw A landed, raw A read (128 arrivals), A operands written (128 arrivals), D chunk
-// landed, chunk products done; then all products done, error drain.  Every waiter steps through a barrier's phases
-// in order from phase 0, and no barrier can run two phases ahead of a waiter.
-enum { B_RAW = 0, B_RAWFREE = 2, B_OP = 4, B_D = 6, B_FREE = 8, B_DONE = 10, B_FIN = 11, NBAR = 12 };
+// landed, chunk products done; then a half's products done, its accumulators read (128 arrivals), error drain.
+// Every waiter steps through a barrier's phases in order from phase 0, and no barrier can run two phases ahead of a
+// waiter.
+enum { B_RAW = 0, B_RAWFREE = 2, B_OP = 4, B_D = 6, B_FREE = 8, B_DONE = 10, B_TFREE = 11, B_FIN = 12, NBAR = 13 };
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 static_assert(TMAP_BOX_COLS == CH && TMAP_BOX_ROWS == ROWS, "one TMA box is one 128-row tile of a chunk");
 __device__ __forceinline__ uint32_t ring_parity(int c) { return (uint32_t)((c >> 1) & 1); }
@@ -48,7 +51,8 @@ __global__ void k_d_image(const float* __restrict__ D_all, int n, char* __restri
 }
 
 __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long long ldq, const char* __restrict__ maps,
-                                                 const char* __restrict__ img_all, int* __restrict__ status) {
+                                                 const char* __restrict__ img_all, float* __restrict__ scratch,
+                                                 int* __restrict__ status) {
     extern __shared__ unsigned char smem_raw[];
     char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     char* const RAW = sm + OFF_RAW;
@@ -61,12 +65,14 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
     const int b = blockIdx.y;
     const int row0 = blockIdx.x * ROWS;
     const int nchunks = n / CH;
+    const int nh = n > 256 ? 2 : 1, N = n / nh;   // column halves and their width
+    const int total = nh * nchunks;               // chunks over all halves: g = h * nchunks + c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (warp == 0) tc::tmem_alloc(tmem_slot, TCOLS);
     if (tid == 0) {
         for (int i = 0; i < NBAR; ++i)
-            tc::mbar_init(&bars[i], (i >= B_RAWFREE && i < B_D) ? 128 : 1);
+            tc::mbar_init(&bars[i], ((i >= B_RAWFREE && i < B_D) || i == B_TFREE) ? 128 : 1);
         tc::mbar_fence_init();
         *err = 0;
     }
@@ -76,14 +82,21 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
     const uint32_t tmem = *tmem_slot;
 
     if (warp < 4) {
-        // ---------------- epilogue: row me, y + acc in place ----------------
-        const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], 0u, 500);
-        if (__all_sync(0xffffffffu, done && !*err)) {   // per warp: tcgen05.ld needs the whole warp
+        // ---------------- epilogue: row me, y + acc per half ----------------
+        const int me = warp * 32 + lane, row = row0 + me;
+        float* qr = (p.tab ? p.tab[b] : p.one).Q + (long long)row * ldq;
+        float* sr = scratch ? scratch + ((size_t)b * K + (size_t)(row < K ? row : 0)) * 256 : nullptr;
+        const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+        for (int h = 0; h < nh; ++h) {
+            const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], (uint32_t)(h & 1), 200);
+            if (!__all_sync(0xffffffffu, done && !*err)) {   // per warp: tcgen05.ld needs the whole warp
+                *err = 1;
+                break;
+            }
             tc::fence_after_sync();
-            const int me = warp * 32 + lane, row = row0 + me;
-            float* qr = (p.tab ? p.tab[b] : p.one).Q + (long long)row * ldq;
-            const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
-            for (int cb = 0; cb < n / 32; ++cb) {
+            const int c0 = h * N;
+            float* dst = (h + 1 < nh) ? sr : qr + c0;   // an earlier half waits in the scratch rows
+            for (int cb = 0; cb < N / 32; ++cb) {
                 float big[32], small[32];
                 tc::tmem_ld32(tl + 32 * cb, big);
                 tc::tmem_ld32(tl + 256 + 32 * cb, small);
@@ -91,20 +104,28 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                 if (row < K) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
-                        float4 y = *reinterpret_cast<const float4*>(qr + 32 * cb + i);
+                        float4 y = *reinterpret_cast<const float4*>(qr + c0 + 32 * cb + i);
                         y.x = __fadd_rn(y.x, __fadd_rn(big[i], small[i]));
                         y.y = __fadd_rn(y.y, __fadd_rn(big[i + 1], small[i + 1]));
                         y.z = __fadd_rn(y.z, __fadd_rn(big[i + 2], small[i + 2]));
                         y.w = __fadd_rn(y.w, __fadd_rn(big[i + 3], small[i + 3]));
-                        *reinterpret_cast<float4*>(qr + 32 * cb + i) = y;   // every product has read this row
+                        *reinterpret_cast<float4*>(dst + 32 * cb + i) = y;
                     }
                 }
             }
+            if (h + 1 < nh) {   // the next half's products may overwrite the accumulators
+                tc::fence_before_sync();
+                tc::mbar_arrive(&bars[B_TFREE]);
+            }
+        }
+        if (nh > 1 && !*err && row < K) {   // every product of every half has read this row: the scratch goes in
+            for (int c = 0; c < N; c += 4)
+                *reinterpret_cast<float4*>(qr + c) = *reinterpret_cast<const float4*>(sr + c);
         }
     } else if (warp < 8) {
         // ---------------- convert: raw Q tile -> tf32 hi | lo, rows 16 i + t / 8, k-quad t % 8 ----------------
         const int t = tid - 128, aq = t & 7, am = t >> 3;
-        for (int c = 0; c < nchunks; ++c) {
+        for (int c = 0; c < total; ++c) {   // c: chunk over all halves
             const int st = c & 1;
             if (*err || !tc::mbar_wait(&bars[B_RAW + st], ring_parity(c))) {
                 *err = 1;
@@ -128,29 +149,32 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
     } else if (warp == 8) {
         // ---------------- products ----------------
         if (lane == 0) {
-            const uint32_t idesc = tc::idesc_tf32(ROWS, n);
+            const uint32_t idesc = tc::idesc_tf32(ROWS, N);
             bool ok = true;
-            for (int c = 0; c < nchunks; ++c) {
-                const int st = c & 1;
-                ok = !*err && tc::mbar_wait_sleep(&bars[B_OP + st], ring_parity(c), 20) &&
-                     tc::mbar_wait(&bars[B_D + st], ring_parity(c));
+            for (int g = 0; g < total; ++g) {
+                const int st = g & 1, c = g % nchunks, h = g / nchunks;
+                if (c == 0 && h > 0) {   // the previous half's accumulators have been read
+                    ok = !*err && tc::mbar_wait_sleep(&bars[B_TFREE], (uint32_t)((h - 1) & 1), 20);
+                    if (!ok) break;
+                }
+                ok = !*err && tc::mbar_wait_sleep(&bars[B_OP + st], ring_parity(g), 20) &&
+                     tc::mbar_wait(&bars[B_D + st], ring_parity(g));
                 if (!ok) break;
                 tc::fence_after_sync();
                 const uint32_t a = tc::smem_u32(AOP + st * 2 * YT), d = tc::smem_u32(DB + st * 2 * DPART);
 #pragma unroll 1
                 for (int k = 0; k < CH / 8; ++k) {
                     const uint64_t ahi = tc::sdesc_k128(a + 32 * k), alo = tc::sdesc_k128(a + YT + 32 * k);
-                    const uint64_t dhi = tc::sdesc_k128(d + 32 * k), dlo = tc::sdesc_k128(d + n * 128 + 32 * k);
+                    const uint64_t dhi = tc::sdesc_k128(d + 32 * k), dlo = tc::sdesc_k128(d + N * 128 + 32 * k);
                     const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
                     tc::mma_tf32(tmem, ahi, dhi, idesc, acc);
                     tc::mma_tf32(tmem + 256, ahi, dlo, idesc, acc);
                     tc::mma_tf32(tmem + 256, alo, dhi, idesc, 1u);
                 }
                 tc::mma_commit(&bars[B_FREE + st]);
+                if (c == nchunks - 1) tc::mma_commit(&bars[B_DONE]);   // this half's products are done
             }
-            if (ok) {
-                tc::mma_commit(&bars[B_DONE]);
-            } else {
+            if (!ok) {
                 *err = 1;
                 tc::mma_commit(&bars[B_FIN]);   // let issued products finish before TMEM is released
                 tc::mbar_wait(&bars[B_FIN], 0u);
@@ -161,23 +185,25 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
         if (lane == 0) {
             const void* map = maps + ((size_t)b * TMAPS_PER_MATRIX + TMAP_Q) * 128;
             const char* img = img_all + (size_t)b * ns_dimg_bytes(n);
-            const uint32_t dbytes = (uint32_t)(2 * n * 128);
+            const uint32_t pbytes = (uint32_t)(N * 128);   // one half's rows of one part (hi or lo) of a D chunk
             tc::tmap_acquire(map);
             int n_raw[2] = {0, 0}, n_d[2] = {0, 0};
             bool ok = true;
-            for (int c = 0; c < nchunks; ++c) {
-                const int st = c & 1;
-                if (c >= 2) {
-                    // raw tile c - 2 read by the convert warps; D chunk c - 2 read by its products
-                    ok = !*err && tc::mbar_wait_sleep(&bars[B_RAWFREE + st], ring_parity(c - 2), 100) &&
-                         tc::mbar_wait_sleep(&bars[B_FREE + st], ring_parity(c - 2), 100);
+            for (int g = 0; g < total; ++g) {
+                const int st = g & 1, c = g % nchunks, h = g / nchunks;
+                if (g >= 2) {
+                    // raw tile g - 2 read by the convert warps; D chunk g - 2 read by its products
+                    ok = !*err && tc::mbar_wait_sleep(&bars[B_RAWFREE + st], ring_parity(g - 2), 100) &&
+                         tc::mbar_wait_sleep(&bars[B_FREE + st], ring_parity(g - 2), 100);
                     if (!ok) break;
                 }
                 tc::mbar_expect_tx(&bars[B_RAW + st], (uint32_t)YT);
                 tc::tma_load_2d(RAW + st * YT, map, c * CH, row0, &bars[B_RAW + st]);
                 ++n_raw[st];
-                tc::mbar_expect_tx(&bars[B_D + st], dbytes);
-                tc::bulk_g2s(DB + st * 2 * DPART, img + (size_t)c * dbytes, dbytes, &bars[B_D + st]);
+                const char* chunk = img + (size_t)c * 2 * n * 128 + (size_t)h * N * 128;
+                tc::mbar_expect_tx(&bars[B_D + st], 2 * pbytes);
+                tc::bulk_g2s(DB + st * 2 * DPART, chunk, pbytes, &bars[B_D + st]);                       // hi rows
+                tc::bulk_g2s(DB + st * 2 * DPART + pbytes, chunk + (size_t)n * 128, pbytes, &bars[B_D + st]);   // lo rows
                 ++n_d[st];
             }
             if (!ok) {
@@ -197,14 +223,15 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
 }
 
 cudaError_t launch_ns_ws(PtrArg p, int K, int n, long long ldq, int B, const float* D, const char* maps, char* img,
-                         int* status, cudaStream_t st) {
-    if (n > 256 || n % CH) return cudaErrorInvalidValue;
+                         float* scratch, int* status, cudaStream_t st) {
+    if (n > 512 || n % CH || (n > 256 && !scratch)) return cudaErrorInvalidValue;
     k_d_image<<<dim3(cdiv(n * n / 4, 256), B), 256, 0, st>>>(D, n, img);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_ns_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    k_ns_ws<<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, status);
+    k_ns_ws<<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, n > 256 ? scratch : nullptr,
+                                                           status);
     return cudaGetLastError();
 }
 

@@ -1,11 +1,10 @@
-// Row-block kernels: the blocked triangular solve Y = (s X + eps Z) L^-T and the Newton-Schulz update Y <- Y + Y D.
+// Row-block kernel for n > 256: the blocked triangular solve Y = (s X + eps Z) L^-T.
 //
-// Each CTA owns BM = 64 rows and keeps them (all n columns) in shared memory for the whole kernel, so both kernels
-// run in place on Q: rows are read once, finished in shared memory, and written once; no other CTA touches them.
+// Each CTA owns BM = 64 rows and keeps them (all n columns) in shared memory for the whole kernel, so it runs in
+// place on Q: rows are read once, finished in shared memory, and written once; no other CTA touches them.
 //
 // trsm follows candidates/tri.py:378-403 (_trsm_f_kernel): 32-column blocks j in order; acc = s x (+ eps z); for each
 // earlier block k, acc -= (Y_k L[j, k]^T) with that dot as one FMA chain; then Y_j = acc Li_j^T.
-// ns_update follows candidates/kcholqr.py:22 (torch.addmm(Y, Y, D)): y + (sum_a y_a D[a, c]), the sum an FMA chain.
 // Thread map: 256 threads = 32 row pairs x 8 column groups of 4; shared rows padded to n + 1 floats (no bank
 // conflicts for the column-group reads).
 #include "kernels.h"
@@ -151,70 +150,12 @@ __global__ void __launch_bounds__(256) k_trsm(PtrArg p, Src src, int K, int n, l
     store_rows(Ys, ldy, mp.Q, ldq, row0, K, n);
 }
 
-__global__ void __launch_bounds__(256) k_ns_update(PtrArg p, int K, int n, long long ldq, const float* __restrict__ D_all) {
-    extern __shared__ __align__(16) float sm[];
-    const int ldy = n + 1;
-    float* Ys = sm;              // [BM][n + 1]
-    float* Dt = Ys + BM * ldy;   // [32][n + 1]: rows c0..c0+31 of D (= its columns, D is symmetric)
-    const int b = blockIdx.y;
-    const MatPtr mp = p.tab ? p.tab[b] : p.one;
-    float* Q = mp.Q;
-    const float* D = D_all + (size_t)b * n * n;
-    const int row0 = blockIdx.x * BM;
-    load_rows(Ys, ldy, Q, ldq, row0, K, n, false, 1.0f, nullptr, 0.0f);
-    const int rp = threadIdx.x >> 3, cg = threadIdx.x & 7;
-    const float* y0 = Ys + (2 * rp) * ldy;
-    const float* y1 = y0 + ldy;
-    const int r0 = row0 + 2 * rp;
-    for (int c0 = 0; c0 < n; c0 += TB) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < TB * n; e += blockDim.x) {
-            const int cl = e / n, a = e - cl * n;
-            Dt[cl * ldy + a] = __ldg(D + (size_t)(c0 + cl) * n + a);
-        }
-        __syncthreads();
-        float acc[2][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[0][i] = acc[1][i] = 0.0f;
-#pragma unroll 8
-        for (int a = 0; a < n; ++a) {
-            const float a0 = y0[a], a1 = y1[a];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float d = Dt[(cg * 4 + i) * ldy + a];
-                acc[0][i] = __fmaf_rn(a0, d, acc[0][i]);
-                acc[1][i] = __fmaf_rn(a1, d, acc[1][i]);
-            }
-        }
-        const int c = c0 + cg * 4;
-        if (r0 < K)
-            *reinterpret_cast<float4*>(Q + (long long)r0 * ldq + c) =
-                make_float4(__fadd_rn(y0[c], acc[0][0]), __fadd_rn(y0[c + 1], acc[0][1]),
-                            __fadd_rn(y0[c + 2], acc[0][2]), __fadd_rn(y0[c + 3], acc[0][3]));
-        if (r0 + 1 < K)
-            *reinterpret_cast<float4*>(Q + (long long)(r0 + 1) * ldq + c) =
-                make_float4(__fadd_rn(y1[c], acc[1][0]), __fadd_rn(y1[c + 1], acc[1][1]),
-                            __fadd_rn(y1[c + 2], acc[1][2]), __fadd_rn(y1[c + 3], acc[1][3]));
-    }
-}
-
-static size_t trsm_smem(int n) { return sizeof(float) * ((size_t)(BM + TB) * (n + 1) + TB * (TB + 1)); }
-static size_t ns_smem(int n) { return sizeof(float) * ((size_t)(BM + TB) * (n + 1)); }
-
 cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
                         ScaleArg sc, float eps, const float* L, const float* Li, cudaStream_t st) {
     const size_t smem = trsm_smem(n);
     cudaError_t e = cudaFuncSetAttribute(k_trsm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     k_trsm<<<dim3(cdiv(K, BM), B), 256, smem, st>>>(p, src, K, n, ldx, ldq, Z, sc, eps, L, Li);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_ns_update(PtrArg p, int K, int n, long long ldq, int B, const float* D, cudaStream_t st) {
-    const size_t smem = ns_smem(n);
-    cudaError_t e = cudaFuncSetAttribute(k_ns_update, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k_ns_update<<<dim3(cdiv(K, BM), B), 256, smem, st>>>(p, K, n, ldq, D);
     return cudaGetLastError();
 }
 

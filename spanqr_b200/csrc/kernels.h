@@ -93,14 +93,13 @@ cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B
 cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
                         ScaleArg sc, float eps, const float* L, const float* Li, cudaStream_t st);
 
-// Q <- Q + Q D per matrix, n <= 256, warp-specialised and fed by TMA (maps from launch_tmaps): D is first split into
-// its operand image `img` (ns_dimg_bytes(n) per matrix); a bounded wait that runs out ORs 0x20 into *status
+// Q <- Q + Q D per matrix, n <= 512, warp-specialised and fed by TMA (maps from launch_tmaps): D is first split into
+// its operand image `img` (ns_dimg_bytes(n) per matrix); for n > 256 `scratch` holds K x 256 floats per matrix; a
+// bounded wait that runs out ORs 0x20 into *status
 __host__ __device__ inline size_t ns_dimg_bytes(int n) { return (size_t)8 * n * n; }
 cudaError_t launch_ns_ws(PtrArg p, int K, int n, long long ldq, int B, const float* D, const char* maps, char* img,
-                         int* status, cudaStream_t st);
+                         float* scratch, int* status, cudaStream_t st);
 
 
-// Q <- Q + Q D per matrix, in place (D symmetric, n x n per matrix)
-cudaError_t launch_ns_update(PtrArg p, int K, int n, long long ldq, int B, const float* D, cudaStream_t st);
 
 }  // namespace spq

@@ -150,6 +150,8 @@ __global__ void __launch_bounds__(256) k_trsm(PtrArg p, Src src, int K, int n, l
     store_rows(Ys, ldy, mp.Q, ldq, row0, K, n);
 }
 
+static size_t trsm_smem(int n) { return sizeof(float) * ((size_t)(BM + TB) * (n + 1) + TB * (TB + 1)); }
+
 cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
                         ScaleArg sc, float eps, const float* L, const float* Li, cudaStream_t st) {
     const size_t smem = trsm_smem(n);

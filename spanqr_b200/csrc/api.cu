@@ -138,7 +138,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         // gram_f is matched closely enough by it: the robustness and span tests pass either way)
         SPQ_TRY(timed(K_GRAM, st, [&] {
             return r <= 256 ? launch_gram_ws(p, first ? SRC_X : SRC_Q, K, r, B, gp, maps, sc, P, status, st)
-                            : launch_gram_tc(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, 0, P, status,
+                            : launch_gram_tc(p, first ? SRC_X : SRC_Q, K, r, first ? ldx : ldq, B, gp, sc, GRAM_PLAIN, P, status,
                                              st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 0, G, rowsq, st); }));
@@ -154,14 +154,14 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         }));
     }
     for (int it = 0; it < NS_STEPS; ++it) {
-        // the last polish step's Gram decides Q's final orthogonality (and with it the span error on the dominant
-        // directions): it keeps the exact three-way split and fp64 drains every 32 rows (gram_split, kcholqr.py:20)
+        // the last polish step's Gram (gram_split, kcholqr.py:20) decides Q's final orthogonality, and with it the
+        // span error on the dominant directions: it drains its large-term accumulator into fp64 every 128 rows
         const bool last = it == NS_STEPS - 1;
         SPQ_TRY(timed(last ? K_GRAM_ACC : K_GRAM, st, [&] {
             return (r <= 256 && !last)
                        ? launch_gram_ws(p, SRC_Q, K, r, B, gp, maps, ScaleArg{nullptr, nullptr}, P, status, st)
-                       : launch_gram_tc(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr}, last ? 1 : 0, P, status,
-                                        st);
+                       : launch_gram_tc(p, SRC_Q, K, r, ldq, B, gp, ScaleArg{nullptr, nullptr},
+                                        last ? GRAM_DRAINED : GRAM_PLAIN, P, status, st);
         }));
         SPQ_TRY(timed(K_REDUCE, st, [&] { return launch_gram_reduce(P, r, B, gp, 1, G, nullptr, st); }));
         // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel
@@ -313,7 +313,7 @@ int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_
     PtrArg p{nullptr, MatPtr{Y, nullptr}};
     cudaError_t e = cudaMemsetAsync(at<int>(ws, l.status), 0, sizeof(int), st);
     if (e == cudaSuccess)
-        e = launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, 1, at<float>(ws, l.P),
+        e = launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, GRAM_ACCURATE, at<float>(ws, l.P),
                            at<int>(ws, l.status), st);
     if (e == cudaSuccess) e = launch_gram_reduce(at<float>(ws, l.P), n, 1, gp, 0, G, nullptr, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);

@@ -424,7 +424,8 @@ static cudaError_t launch_parts(PtrArg p, Src src, int K, int n, long long ld, i
 
 cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
                            int accurate, float* P, int* status, cudaStream_t st) {
-    if (accurate) return launch_parts<3>(p, src, K, n, ld, B, gp, sc, P, status, st);
+    if (accurate == GRAM_ACCURATE) return launch_parts<3>(p, src, K, n, ld, B, gp, sc, P, status, st);
+    if (accurate == GRAM_DRAINED) return launch_parts<2>(p, src, K, n, ld, B, gp, sc, P, status, st);
     cudaError_t e = cudaFuncSetAttribute(k_gram_tc_plain, cudaFuncAttributeMaxDynamicSharedMemorySize, PLAIN_SMEM);
     if (e != cudaSuccess) return e;
     k_gram_tc_plain<<<dim3(gp.tiles, gp.S, B), PLAIN_NT, PLAIN_SMEM, st>>>(p, src, K, n, ld, gp, sc, P, status);

@@ -2,8 +2,9 @@
 // tensor cores, 3xTF32 (hi.hi into one TMEM accumulator, hi.lo + lo.hi into a second).
 //
 // k_d_image splits D (symmetric, from k_gram_reduce) once per matrix into tf32 hi/lo operand tiles laid out as the
-// update's shared-memory B operand: for each chunk of 32 contraction indices, rows c = 0..n-1 (row c of D is column
-// c) x 32 k, K-major with the 128-byte swizzle, hi part then lo part.  k_ns_ws then streams those chunks by bulk copy.
+// update's shared-memory B operand: for each chunk of 32 contraction indices and each column half, the half's rows c
+// (row c of D is column c) x 32 k, K-major with the 128-byte swizzle, hi part then lo part, so that k_ns_ws streams
+// each chunk of each half with one bulk copy.
 // One CTA = 128 rows of one matrix, all n output columns, in nh = 1 (n <= 256) or 2 column halves of N = n / nh
 // (TMEM holds the large and small accumulators of at most 256 columns); warp roles: 0-3 epilogue (TMEM lanes = rows:
 // y + acc), 4-7 convert (raw 32-column tile of Q by TMA -> tf32 hi | lo, K-major), 8 products (one thread, fixed
@@ -45,11 +46,13 @@ __global__ void k_d_image(const float* __restrict__ D_all, int n, char* __restri
     const int nq = n / 4;
     if (e >= n * nq) return;
     const int c = e / nq, kq = e % nq, kc = kq / 8, q = kq % 8;
+    const int N = n > 256 ? n / 2 : n, h = c / N, rr = c % N;   // column half and row within it
     const float4 v = *reinterpret_cast<const float4*>(D_all + (size_t)b * n * n + (size_t)c * n + 4 * kq);
-    char* part = img_all + (size_t)b * ns_dimg_bytes(n) + (size_t)kc * 2 * n * 128;
-    tc::store2_at(part, part + (size_t)n * 128, tc::swz_off(c, q), v);
+    char* part = img_all + (size_t)b * ns_dimg_bytes(n) + (size_t)kc * 2 * n * 128 + (size_t)h * 2 * N * 128;
+    tc::store2_at(part, part + (size_t)N * 128, tc::swz_off(rr, q), v);
 }
 
+template <int NH>   // column halves: 1 for n <= 256, 2 above
 __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long long ldq, const char* __restrict__ maps,
                                                  const char* __restrict__ img_all, float* __restrict__ scratch,
                                                  int* __restrict__ status) {
@@ -65,7 +68,8 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
     const int b = blockIdx.y;
     const int row0 = blockIdx.x * ROWS;
     const int nchunks = n / CH;
-    const int nh = n > 256 ? 2 : 1, N = n / nh;   // column halves and their width
+    constexpr int nh = NH;
+    const int N = n / nh;                         // width of a column half
     const int total = nh * nchunks;               // chunks over all halves: g = h * nchunks + c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -88,14 +92,14 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
         float* sr = scratch ? scratch + ((size_t)b * K + (size_t)(row < K ? row : 0)) * 256 : nullptr;
         const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
         for (int h = 0; h < nh; ++h) {
-            const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], (uint32_t)(h & 1), 200);
+            const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], (uint32_t)(h & 1), 500);
             if (!__all_sync(0xffffffffu, done && !*err)) {   // per warp: tcgen05.ld needs the whole warp
                 *err = 1;
                 break;
             }
             tc::fence_after_sync();
             const int c0 = h * N;
-            float* dst = (h + 1 < nh) ? sr : qr + c0;   // an earlier half waits in the scratch rows
+            float* dst = (nh > 1 && h + 1 < nh) ? sr : qr + c0;   // an earlier half waits in the scratch rows
             for (int cb = 0; cb < N / 32; ++cb) {
                 float big[32], small[32];
                 tc::tmem_ld32(tl + 32 * cb, big);
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                     }
                 }
             }
-            if (h + 1 < nh) {   // the next half's products may overwrite the accumulators
+            if (nh > 1 && h + 1 < nh) {   // the next half's products may overwrite the accumulators
                 tc::fence_before_sync();
                 tc::mbar_arrive(&bars[B_TFREE]);
             }
@@ -152,8 +156,8 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
             const uint32_t idesc = tc::idesc_tf32(ROWS, N);
             bool ok = true;
             for (int g = 0; g < total; ++g) {
-                const int st = g & 1, c = g % nchunks, h = g / nchunks;
-                if (c == 0 && h > 0) {   // the previous half's accumulators have been read
+                const int st = g & 1, h = (nh > 1 && g >= nchunks) ? 1 : 0, c = g - h * nchunks;
+                if (nh > 1 && c == 0 && h > 0) {   // the previous half's accumulators have been read
                     ok = !*err && tc::mbar_wait_sleep(&bars[B_TFREE], (uint32_t)((h - 1) & 1), 20);
                     if (!ok) break;
                 }
@@ -190,7 +194,7 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
             int n_raw[2] = {0, 0}, n_d[2] = {0, 0};
             bool ok = true;
             for (int g = 0; g < total; ++g) {
-                const int st = g & 1, c = g % nchunks, h = g / nchunks;
+                const int st = g & 1, h = (nh > 1 && g >= nchunks) ? 1 : 0, c = g - h * nchunks;
                 if (g >= 2) {
                     // raw tile g - 2 read by the convert warps; D chunk g - 2 read by its products
                     ok = !*err && tc::mbar_wait_sleep(&bars[B_RAWFREE + st], ring_parity(g - 2), 100) &&
@@ -200,10 +204,9 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                 tc::mbar_expect_tx(&bars[B_RAW + st], (uint32_t)YT);
                 tc::tma_load_2d(RAW + st * YT, map, c * CH, row0, &bars[B_RAW + st]);
                 ++n_raw[st];
-                const char* chunk = img + (size_t)c * 2 * n * 128 + (size_t)h * N * 128;
+                const char* chunk = img + (size_t)c * 2 * n * 128 + (size_t)h * 2 * pbytes;   // hi rows, then lo rows
                 tc::mbar_expect_tx(&bars[B_D + st], 2 * pbytes);
-                tc::bulk_g2s(DB + st * 2 * DPART, chunk, pbytes, &bars[B_D + st]);                       // hi rows
-                tc::bulk_g2s(DB + st * 2 * DPART + pbytes, chunk + (size_t)n * 128, pbytes, &bars[B_D + st]);   // lo rows
+                tc::bulk_g2s(DB + st * 2 * DPART, chunk, 2 * pbytes, &bars[B_D + st]);
                 ++n_d[st];
             }
             if (!ok) {
@@ -228,10 +231,15 @@ cudaError_t launch_ns_ws(PtrArg p, int K, int n, long long ldq, int B, const flo
     k_d_image<<<dim3(cdiv(n * n / 4, 256), B), 256, 0, st>>>(D, n, img);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(k_ns_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    k_ns_ws<<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, n > 256 ? scratch : nullptr,
-                                                           status);
+    if (n > 256) {
+        e = cudaFuncSetAttribute(k_ns_ws<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        k_ns_ws<2><<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, scratch, status);
+    } else {
+        e = cudaFuncSetAttribute(k_ns_ws<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        k_ns_ws<1><<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, nullptr, status);
+    }
     return cudaGetLastError();
 }
 

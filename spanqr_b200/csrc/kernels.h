@@ -58,7 +58,11 @@ cudaError_t launch_tmaps(PtrArg p, int K, int r, long long ldx, long long ldq, i
 // P[b][split][tile][128][128]; a bounded wait that runs out ORs 0x10 into *status
 constexpr int GRAM_TC_SPLIT = 512;
 GramPlan gram_tc_plan(int K, int n);
-// accurate: exact three-way split and six products (the reference's compensated Grams); else two-way, three products
+// mode GRAM_ACCURATE: exact three-way split and six products, the large-term accumulator drained into fp64 every 32
+// rows (the reference's compensated Grams, for the component entry point); GRAM_DRAINED: two-way split, three
+// products, drained every 128 rows (the last polish step: without the drains its truncating accumulation costs
+// orthogonality); GRAM_PLAIN: two-way split, the whole split accumulated in TMEM
+enum { GRAM_PLAIN = 0, GRAM_ACCURATE = 1, GRAM_DRAINED = 2 };
 cudaError_t launch_gram_tc(PtrArg p, Src src, int K, int n, long long ld, int B, const GramPlan& gp, ScaleArg sc,
                            int accurate, float* P, int* status, cudaStream_t st);
 // the two-way-split Gram for n <= 256, warp-specialised and fed by TMA (maps from launch_tmaps): one CTA per 128-row

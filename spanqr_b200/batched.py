@@ -92,8 +92,22 @@ def _run_group(Xs, Qs, stream):
                f"orth_batched({B}x{K}x{r})")
 
 
+SPLIT_MIN = 16   # a shape group of at least this many matrices runs as NSTREAMS parts on as many streams
+NSTREAMS = 4
+_SIDE = {}
+
+
+def _side_streams(dev, n):
+    key = (str(dev), n)
+    if key not in _SIDE:
+        _SIDE[key] = tuple(torch.cuda.Stream(dev) for _ in range(n))
+    return _SIDE[key]
+
+
 def _run_local(Xs, Qs):
-    """orth of a list of matrices on this GPU, one library call per shape"""
+    """orth of a list of matrices on this GPU, one library call per shape.  A large same-shape group is cut in
+    NSTREAMS parts that run on as many streams: many kernels leave SMs idle (one Cholesky CTA per matrix, partial last
+    waves), and the other parts' kernels fill them.  Each matrix's arithmetic does not depend on the grouping."""
     if not Xs:
         return
     dev = Xs[0].device
@@ -104,7 +118,18 @@ def _run_local(Xs, Qs):
         groups[tuple(x.shape)][0].append(x)
         groups[tuple(x.shape)][1].append(q)
     for xs, qs in groups.values():
-        _run_group(xs, qs, stream)
+        if len(xs) < SPLIT_MIN:
+            _run_group(xs, qs, stream)
+            continue
+        side = _side_streams(dev, NSTREAMS)
+        cuts = [len(xs) * i // NSTREAMS for i in range(NSTREAMS + 1)]
+        for s, a, b in zip(side, cuts[:-1], cuts[1:]):
+            s.wait_stream(stream)
+            for t in xs[a:b] + qs[a:b]:
+                t.record_stream(s)   # the caller may drop them before the side stream is done
+            _run_group(xs[a:b], qs[a:b], s)
+        for s in side:
+            stream.wait_stream(s)
 
 
 def _check_host(X, name):

@@ -42,6 +42,16 @@ def test_batched_equals_single_bitwise():
         assert all(_bits(a, b) for a, b in zip(got, single))
 
 
+def test_batched_split_over_streams_equals_single_bitwise():
+    """a group large enough to run in parts on several streams gives every matrix the bits of a lone orth"""
+    from spanqr_b200 import batched
+    Xs = [cases.cfg3_matrix(i, K=640).cuda() for i in range(batched.SPLIT_MIN + 5)]
+    single = [orth(x) for x in Xs]
+    got = orth_batched(Xs)
+    torch.cuda.synchronize()
+    assert all(_bits(a, b) for a, b in zip(got, single))
+
+
 def test_host_inputs_pipelined_match_device_bitwise():
     """CPU inputs: copies in, kernels and copies out overlapped chunk by chunk; same bits as the device path"""
     Xs = [cases.cfg3_matrix(i, K=1024).pin_memory() for i in range(11)]

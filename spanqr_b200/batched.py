@@ -140,43 +140,52 @@ def _check_host(X, name):
         raise ValueError(f"unsupported shape {K}x{r}: r must be a multiple of {TB} in [{TB}, {MAX_R}] and K >= r")
 
 
+HOST_SLOTS = 4        # device buffers in flight in the host path
+HOST_COMPUTE = 2      # compute streams in the host path (consecutive chunks' kernels overlap)
+
+
 def _run_host(Xs, Qs, device, chunks):
-    """Qs[i] = orth(Xs[i]) for CPU tensors, copies in and out overlapped with the kernels (see the module docstring)"""
+    """Qs[i] = orth(Xs[i]) for CPU tensors, copies in and out overlapped with the kernels (see the module docstring):
+    chunk k is copied in on one stream, computed on compute stream k % HOST_COMPUTE and copied out on a third, in
+    device buffer slot k % HOST_SLOTS"""
     cur = torch.cuda.current_stream(device)
-    s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
-    for s in (s_in, s_cmp, s_out):
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    s_cmp = [torch.cuda.Stream(device) for _ in range(HOST_COMPUTE)]
+    for s in [s_in, s_out] + s_cmp:
         s.wait_stream(cur)
     groups = {}
     for i, x in enumerate(Xs):
         groups.setdefault(tuple(x.shape), []).append(i)
     last = None
     for (K, r), idx in groups.items():
-        zdust(K, r, device)   # drawn on the current stream, which the three streams follow
+        zdust(K, r, device)   # drawn on the current stream, which every stream here follows
         nch = max(1, min(chunks, len(idx)))
         step = -(-len(idx) // nch)
         parts = [idx[k:k + step] for k in range(0, len(idx), step)]
-        din = [torch.empty((step, K, r), dtype=torch.float32, device=device) for _ in range(2)]
-        dout = [torch.empty((step, K, r), dtype=torch.float32, device=device) for _ in range(2)]
+        nslot = min(HOST_SLOTS, len(parts))
+        din = [torch.empty((step, K, r), dtype=torch.float32, device=device) for _ in range(nslot)]
+        dout = [torch.empty((step, K, r), dtype=torch.float32, device=device) for _ in range(nslot)]
         for t in din + dout:
-            for s in (s_in, s_cmp, s_out):
+            for s in [s_in, s_out] + s_cmp:
                 t.record_stream(s)
         ev_out = []
         for k, part in enumerate(parts):
-            slot = k % 2
+            slot = k % nslot
             with torch.cuda.stream(s_in):
-                if k >= 2:
-                    s_in.wait_event(ev_out[k - 2])   # chunk k-2 is computed and copied out: its buffers are free
+                if k >= nslot:
+                    s_in.wait_event(ev_out[k - nslot])   # chunk k - nslot is copied out: its slot is free
                 for j, i in enumerate(part):
                     din[slot][j].copy_(Xs[i], non_blocking=True)
                 ev_in = torch.cuda.Event()
                 ev_in.record(s_in)
-            with torch.cuda.stream(s_cmp):
-                s_cmp.wait_event(ev_in)
-                if k >= 2:
-                    s_cmp.wait_event(ev_out[k - 2])
-                _run_group([din[slot][j] for j in range(len(part))], [dout[slot][j] for j in range(len(part))], s_cmp)
+            sc = s_cmp[k % len(s_cmp)]
+            with torch.cuda.stream(sc):
+                sc.wait_event(ev_in)
+                if k >= nslot:
+                    sc.wait_event(ev_out[k - nslot])
+                _run_group([din[slot][j] for j in range(len(part))], [dout[slot][j] for j in range(len(part))], sc)
                 ev_cmp = torch.cuda.Event()
-                ev_cmp.record(s_cmp)
+                ev_cmp.record(sc)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_cmp)
                 for j, i in enumerate(part):

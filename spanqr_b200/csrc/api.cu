@@ -81,9 +81,10 @@ Layout layout(int K, int r, int B) {
     l.G = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.L = o;       o += al256(sizeof(float) * (size_t)B * r * r);
     l.Li = o;      o += al256(sizeof(float) * (size_t)B * r * TB);
-    l.W = o;       o += (r <= 256) ? al256(trsm_w_bytes(r) * (size_t)B) : 0;
+    l.W = o;       o += al256(trsm_w_bytes(r) * (size_t)B);
     l.maps = o;    o += al256((size_t)TMAPS_PER_MATRIX * 128 * B);
-    l.nss = o;     o += (r > 256) ? al256(sizeof(float) * (size_t)B * K * 256) : 0;   // polish update, first half
+    // r > 256: the solve's second-panel start, later the polish update's first half
+    l.nss = o;     o += (r > 256) ? al256(sizeof(float) * (size_t)B * K * 256) : 0;
     // the Gram's split partials; the polish step's D image reuses them once they are reduced
     size_t pbytes = sizeof(float) * (size_t)B * gp.S * gp.tiles * GRAM_TILE * GRAM_TILE;
     if (ns_dimg_bytes(r) * B > pbytes) pbytes = ns_dimg_bytes(r) * B;
@@ -108,6 +109,27 @@ int check_ws(void* ws, size_t ws_bytes, int K, int r, int B) {
 
 template <typename T>
 T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
+
+// The solve on the tensor cores: one panel for n <= 256; for n > 256 the first 8 blocks, the product of those with
+// the W tiles below them (the second panel's start) and the second panel.
+cudaError_t run_trsm(PtrArg p, Src src, int K, int n, long long ldq, int B, const char* maps, const float* Z,
+                     ScaleArg sc, float eps, const char* W, float* scratch, int* status, cudaStream_t st) {
+    const int nb = n / TB;
+    if (nb <= 8)
+        return timed(K_TRSM, st, [&] {
+            return launch_trsm_tc(p, src, K, n, ldq, B, 0, nb, nullptr, maps, Z, sc, eps, W, status, st);
+        });
+    cudaError_t e = timed(K_TRSM, st, [&] {
+        return launch_trsm_tc(p, src, K, n, ldq, B, 0, 8, nullptr, maps, Z, sc, eps, W, status, st);
+    });
+    if (e == cudaSuccess)
+        e = timed(K_TRSM, st, [&] { return launch_trsm_panel_product(p, K, n, ldq, B, 8, nb - 8, maps, W, scratch, status, st); });
+    if (e == cudaSuccess)
+        e = timed(K_TRSM, st, [&] {
+            return launch_trsm_tc(p, src, K, n, ldq, B, 8, nb - 8, scratch, maps, Z, sc, eps, W, status, st);
+        });
+    return e;
+}
 
 // The pass sequence of kcholqr_f for B matrices whose pointers are in the workspace table (filled by k_setup_*).
 int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, void* ws, cudaStream_t st) {
@@ -145,13 +167,9 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         SPQ_TRY(timed(K_CHOL, st, [&] {
             return launch_chol(G, Lm, Li, r, B, rowsq, gram_sq_parts(gp), nullptr, scal + (size_t)pass * B, 0, st);
         }));
-        if (r <= 256) SPQ_TRY(timed(K_TRSM_W, st, [&] { return launch_trsm_w(Lm, Li, r, B, W, st); }));
-        SPQ_TRY(timed(K_TRSM, st, [&] {
-            return r <= 256 ? launch_trsm_tc(p, first ? SRC_X : SRC_Q, K, r, ldq, B, maps, first ? Z : nullptr, sc,
-                                             first ? EPS : 0.0f, W, status, st)
-                            : launch_trsm(p, first ? SRC_X : SRC_Q, K, r, ldx, ldq, B, first ? Z : nullptr, sc,
-                                          first ? EPS : 0.0f, Lm, Li, st);
-        }));
+        SPQ_TRY(timed(K_TRSM_W, st, [&] { return launch_trsm_w(Lm, Li, r, B, W, st); }));
+        SPQ_TRY(run_trsm(p, first ? SRC_X : SRC_Q, K, r, ldq, B, maps, first ? Z : nullptr, sc, first ? EPS : 0.0f, W,
+                         at<float>(ws, l.nss), status, st));
     }
     for (int it = 0; it < NS_STEPS; ++it) {
         // the last polish step's Gram (gram_split, kcholqr.py:20) decides Q's final orthogonality, and with it the
@@ -345,12 +363,11 @@ int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     PtrArg p{nullptr, MatPtr{X, Y}};
     cudaError_t e = cudaMemsetAsync(at<int>(ws, l.status), 0, sizeof(int), st);
-    if (e == cudaSuccess && n <= 256) e = launch_trsm_w(L, Li, n, 1, at<char>(ws, l.W), st);
-    if (e == cudaSuccess && n <= 256) e = launch_tmaps(p, K, n, ldx, ldy, 1, ws, at<char>(ws, l.maps), st);
+    if (e == cudaSuccess) e = launch_trsm_w(L, Li, n, 1, at<char>(ws, l.W), st);
+    if (e == cudaSuccess) e = launch_tmaps(p, K, n, ldx, ldy, 1, ws, at<char>(ws, l.maps), st);
     if (e == cudaSuccess)
-        e = n <= 256 ? launch_trsm_tc(p, SRC_X, K, n, ldy, 1, at<char>(ws, l.maps), Z, ScaleArg{nullptr, d_s},
-                                      Z ? eps : 0.0f, at<char>(ws, l.W), at<int>(ws, l.status), st)
-                     : launch_trsm(p, SRC_X, K, n, ldx, ldy, 1, Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f, L, Li, st);
+        e = run_trsm(p, SRC_X, K, n, ldy, 1, at<char>(ws, l.maps), Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f,
+                     at<char>(ws, l.W), at<float>(ws, l.nss), at<int>(ws, l.status), st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 

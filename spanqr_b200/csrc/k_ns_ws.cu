@@ -9,7 +9,10 @@
 // (TMEM holds the large and small accumulators of at most 256 columns); warp roles: 0-3 epilogue (TMEM lanes = rows:
 // y + acc), 4-7 convert (raw 32-column tile of Q by TMA -> tf32 hi | lo, K-major), 8 products (one thread, fixed
 // order), 9 copies (one thread).  The last half is written in place; an earlier half still feeds the later halves'
-// products, so its new values wait in `scratch` and are copied in after the last half.  Accuracy: |Q D| is about 1e-2 |Q| or less, so 3xTF32 and the
+// products, so its new values wait in `scratch` and are copied in after the last half.
+// Product mode (MODE 1, for the triangular solve of n > 256): the same pipeline computes only the accumulator
+// sum_{k < j0} Y_k [W_{j0, k}; ...; W_{j0+nbp-1, k}]^T from the solve's W image (A = the first 32 j0 columns of Q,
+// B = the stacked W tiles of block column k) and writes it to `scratch` (K x 256 per matrix).  Accuracy: |Q D| is about 1e-2 |Q| or less, so 3xTF32 and the
 // truncating fp32 accumulation leave errors below one ulp of Q.
 #include "kernels.h"
 #include "tc.cuh"
@@ -52,10 +55,10 @@ __global__ void k_d_image(const float* __restrict__ D_all, int n, char* __restri
     tc::store2_at(part, part + (size_t)N * 128, tc::swz_off(rr, q), v);
 }
 
-template <int NH>   // column halves: 1 for n <= 256, 2 above
+template <int NH, int MODE>   // NH: column halves (1 for n <= 256, 2 above); MODE: 0 update, 1 solve panel product
 __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long long ldq, const char* __restrict__ maps,
                                                  const char* __restrict__ img_all, float* __restrict__ scratch,
-                                                 int* __restrict__ status) {
+                                                 int* __restrict__ status, int ncontr, int Nout, int j0) {
     extern __shared__ unsigned char smem_raw[];
     char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     char* const RAW = sm + OFF_RAW;
@@ -67,9 +70,9 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
 
     const int b = blockIdx.y;
     const int row0 = blockIdx.x * ROWS;
-    const int nchunks = n / CH;
+    const int nchunks = ncontr / CH;              // chunks of the contraction
     constexpr int nh = NH;
-    const int N = n / nh;                         // width of a column half
+    const int N = Nout;                           // width of a column half (MODE 1: of the panel product)
     const int total = nh * nchunks;               // chunks over all halves: g = h * nchunks + c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -99,13 +102,19 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
             }
             tc::fence_after_sync();
             const int c0 = h * N;
-            float* dst = (nh > 1 && h + 1 < nh) ? sr : qr + c0;   // an earlier half waits in the scratch rows
+            float* dst = (MODE == 1 || (nh > 1 && h + 1 < nh)) ? sr : qr + c0;   // an earlier half waits in scratch
             for (int cb = 0; cb < N / 32; ++cb) {
                 float big[32], small[32];
                 tc::tmem_ld32(tl + 32 * cb, big);
                 tc::tmem_ld32(tl + 256 + 32 * cb, small);
                 tc::tmem_wait_ld();
-                if (row < K) {
+                if (MODE == 1 && row < K) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4*>(dst + 32 * cb + i) =
+                            make_float4(__fadd_rn(big[i], small[i]), __fadd_rn(big[i + 1], small[i + 1]),
+                                        __fadd_rn(big[i + 2], small[i + 2]), __fadd_rn(big[i + 3], small[i + 3]));
+                } else if (row < K) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
                         float4 y = *reinterpret_cast<const float4*>(qr + c0 + 32 * cb + i);
@@ -122,7 +131,7 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                 tc::mbar_arrive(&bars[B_TFREE]);
             }
         }
-        if (nh > 1 && !*err && row < K) {   // every product of every half has read this row: the scratch goes in
+        if (MODE == 0 && nh > 1 && !*err && row < K) {   // every half's products have read this row: scratch goes in
             for (int c = 0; c < N; c += 4)
                 *reinterpret_cast<float4*>(qr + c) = *reinterpret_cast<const float4*>(sr + c);
         }
@@ -188,7 +197,7 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
         // ---------------- copies ----------------
         if (lane == 0) {
             const void* map = maps + ((size_t)b * TMAPS_PER_MATRIX + TMAP_Q) * 128;
-            const char* img = img_all + (size_t)b * ns_dimg_bytes(n);
+            const char* img = img_all + (size_t)b * (MODE == 0 ? ns_dimg_bytes(n) : wcol_off(n / CH, n / CH));
             const uint32_t pbytes = (uint32_t)(N * 128);   // one half's rows of one part (hi or lo) of a D chunk
             tc::tmap_acquire(map);
             int n_raw[2] = {0, 0}, n_d[2] = {0, 0};
@@ -204,9 +213,17 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                 tc::mbar_expect_tx(&bars[B_RAW + st], (uint32_t)YT);
                 tc::tma_load_2d(RAW + st * YT, map, c * CH, row0, &bars[B_RAW + st]);
                 ++n_raw[st];
-                const char* chunk = img + (size_t)c * 2 * n * 128 + (size_t)h * 2 * pbytes;   // hi rows, then lo rows
                 tc::mbar_expect_tx(&bars[B_D + st], 2 * pbytes);
-                tc::bulk_g2s(DB + st * 2 * DPART, chunk, 2 * pbytes, &bars[B_D + st]);
+                if (MODE == 0) {
+                    const char* chunk = img + (size_t)c * 2 * n * 128 + (size_t)h * 2 * pbytes;   // hi rows, lo rows
+                    tc::bulk_g2s(DB + st * 2 * DPART, chunk, 2 * pbytes, &bars[B_D + st]);
+                } else {
+                    // block column c of the W image: tiles j0 .. of its trailing list (hi), and the same in the lo list
+                    const int NB = n / CH;
+                    const char* hi = img + wcol_off(NB, c) + 2 * 4096 + (size_t)(j0 - c - 1) * 4096;
+                    tc::bulk_g2s(DB + st * 2 * DPART, hi, pbytes, &bars[B_D + st]);
+                    tc::bulk_g2s(DB + st * 2 * DPART + pbytes, hi + (size_t)(NB - 1 - c) * 4096, pbytes, &bars[B_D + st]);
+                }
                 ++n_d[st];
             }
             if (!ok) {
@@ -225,22 +242,30 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
     if (warp == 0) tc::tmem_dealloc(tmem, TCOLS);
 }
 
+template <int NH, int MODE>
+static cudaError_t launch_k(PtrArg p, int K, int n, long long ldq, int B, const char* maps, const char* img,
+                            float* scratch, int* status, int ncontr, int N, int j0, cudaStream_t st) {
+    cudaError_t e = cudaFuncSetAttribute(k_ns_ws<NH, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    k_ns_ws<NH, MODE><<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, scratch, status, ncontr,
+                                                                     N, j0);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_ns_ws(PtrArg p, int K, int n, long long ldq, int B, const float* D, const char* maps, char* img,
                          float* scratch, int* status, cudaStream_t st) {
     if (n > 512 || n % CH || (n > 256 && !scratch)) return cudaErrorInvalidValue;
     k_d_image<<<dim3(cdiv(n * n / 4, 256), B), 256, 0, st>>>(D, n, img);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (n > 256) {
-        e = cudaFuncSetAttribute(k_ns_ws<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        k_ns_ws<2><<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, scratch, status);
-    } else {
-        e = cudaFuncSetAttribute(k_ns_ws<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        k_ns_ws<1><<<dim3(cdiv(K, ROWS), B), NT, SMEM_BYTES, st>>>(p, K, n, ldq, maps, img, nullptr, status);
-    }
-    return cudaGetLastError();
+    return n > 256 ? launch_k<2, 0>(p, K, n, ldq, B, maps, img, scratch, status, n, n / 2, 0, st)
+                   : launch_k<1, 0>(p, K, n, ldq, B, maps, img, nullptr, status, n, n, 0, st);
+}
+
+cudaError_t launch_trsm_panel_product(PtrArg p, int K, int n, long long ldq, int B, int j0, int nbp, const char* maps,
+                                      const char* W, float* scratch, int* status, cudaStream_t st) {
+    if (n > 512 || n % CH || j0 < 1 || nbp < 1 || nbp > 8 || (j0 + nbp) * CH > n || !scratch) return cudaErrorInvalidValue;
+    return launch_k<1, 1>(p, K, n, ldq, B, maps, W, scratch, status, j0 * CH, nbp * CH, j0, st);
 }
 
 }  // namespace spq

@@ -16,6 +16,9 @@
 //   warp 9     one thread issues every copy: row tiles through the per-matrix tensor maps, W tiles by bulk copy (a
 //              copy can hold its issuing thread for a microsecond, which must not delay the products).
 // The output block j is written to Q (in place in passes 2 and 3: block j was read before, later blocks are untouched).
+// One launch solves one panel of at most 8 blocks, j0 .. j0 + nbp - 1, of a matrix of NB = n / 32 blocks (W indexed in
+// the whole image); a second panel starts its accumulators from `init`, the first panel's contribution
+// sum_{k < j0} Y_k W_jk^T computed by k_ns_ws in its product mode.
 #include <cstring>
 
 #include "kernels.h"
@@ -50,7 +53,8 @@ static_assert(TMAP_BOX_COLS == BLK && TMAP_BOX_ROWS == ROWS, "one TMA tile is on
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 }  // namespace
 
-__global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq,
+__global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int j0, int nbp,
+                                                   const float* __restrict__ init,
                                                    const char* __restrict__ maps, const __grid_constant__ CUtensorMap zmap,
                                                    int has_z, ScaleArg sc, float eps, const char* __restrict__ W_all,
                                                    int* __restrict__ status) {
@@ -66,7 +70,8 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
 
     const int b = blockIdx.y;
     const int row0 = blockIdx.x * ROWS;
-    const int nb = n / BLK;
+    const int NB = n / BLK;   // blocks of the matrix (W image)
+    const int nb = nbp;       // blocks of this panel, j0 .. j0 + nb - 1; local index c <-> block j0 + c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (warp == 0) tc::tmem_alloc(tmem_slot, TCOLS);
@@ -83,9 +88,23 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
     if (warp < 4) {
         // ---------------- epilogue warps: row me of the CTA ----------------
         const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
-        // every product adds to its accumulator: start them all at zero
+        // every product adds to its accumulator: start them at zero, or the large ones at `init` (this row)
 #pragma unroll 1
-        for (int c = 0; c < (int)TCOLS; c += 32) tc::tmem_st32_zero(tlane + (uint32_t)c);
+        for (int c = 0; c < (int)TCOLS; c += 32) {
+            if (init && c < 32 * nb) {
+                const int row = row0 + warp * 32 + lane;
+                float v[32];
+                const float* ir = init + ((size_t)b * K + (row < K ? row : 0)) * 256 + c;
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    const float4 x = row < K ? *reinterpret_cast<const float4*>(ir + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
+                }
+                tc::tmem_st32(tlane + (uint32_t)c, v);
+            } else {
+                tc::tmem_st32_zero(tlane + (uint32_t)c);
+            }
+        }
         tc::tmem_wait_st();
         tc::fence_before_sync();
         tc::bar_sync(2, 128 + 32);   // with the issue warp: accumulators zeroed before the first product
@@ -115,7 +134,7 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
             if (rowe < K) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
-                    *reinterpret_cast<float4*>(qrow + 32 * j + 4 * q) =
+                    *reinterpret_cast<float4*>(qrow + 32 * (j0 + j) + 4 * q) =
                         make_float4(big[4 * q], big[4 * q + 1], big[4 * q + 2], big[4 * q + 3]);
             }
         }
@@ -213,28 +232,35 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
         // ---------------- copy warp ----------------
         if (lane == 0) {
             const void* amap = maps + ((size_t)b * TMAPS_PER_MATRIX + (src == SRC_X ? TMAP_X : TMAP_Q)) * 128;
-            const char* Wimg = W_all + (size_t)b * wcol_off(nb, nb);
+            const char* Wimg = W_all + (size_t)b * wcol_off(NB, NB);
             tc::tmap_acquire(amap);
             int n_a[2] = {0, 0}, n_wd[2] = {0, 0}, n_wt[2] = {0, 0};
             auto issue_a = [&](int c) {   // raw A_c into A buffer c % 2: x tile, and z tile behind it in the first pass
                 uint64_t* bar = &bars[B_A + (c & 1)];
                 char* dst = AB + (c & 1) * 2 * YT;
                 tc::mbar_expect_tx(bar, has_z ? 2 * YT : YT);
-                tc::tma_load_2d(dst, amap, c * BLK, row0, bar);
-                if (has_z) tc::tma_load_2d(dst + YT, &zmap, c * BLK, row0, bar);
+                tc::tma_load_2d(dst, amap, (j0 + c) * BLK, row0, bar);
+                if (has_z) tc::tma_load_2d(dst + YT, &zmap, (j0 + c) * BLK, row0, bar);
                 ++n_a[c & 1];
             };
             auto issue_wd = [&](int c) {
                 uint64_t* bar = &bars[B_WD + (c & 1)];
                 tc::mbar_expect_tx(bar, 2 * WPART);
-                tc::bulk_g2s(WD + (c & 1) * 2 * WPART, Wimg + wcol_off(nb, c), 2 * WPART, bar);
+                tc::bulk_g2s(WD + (c & 1) * 2 * WPART, Wimg + wcol_off(NB, j0 + c), 2 * WPART, bar);
                 ++n_wd[c & 1];
             };
-            auto issue_wt = [&](int c) {   // W_{c+1 .. nb-1, c}, c <= nb - 2
-                const uint32_t bytes = (uint32_t)(nb - 1 - c) * 2 * WPART;
+            auto issue_wt = [&](int c) {   // W_{c+1 .. nb-1, c} of the panel (local indices), c <= nb - 2
+                const int g = j0 + c, t = nb - 1 - c;   // the column's trailing tiles in the panel: the first t
                 uint64_t* bar = &bars[B_WT + (c & 1)];
-                tc::mbar_expect_tx(bar, bytes);
-                tc::bulk_g2s(WT + (c & 1) * WTBUF, Wimg + wcol_off(nb, c) + 2 * WPART, bytes, bar);
+                const char* hi = Wimg + wcol_off(NB, g) + 2 * WPART;
+                tc::mbar_expect_tx(bar, (uint32_t)t * 2 * WPART);
+                if (NB - 1 - g == t) {   // the panel runs to the last block: hi and lo tiles adjacent, one copy
+                    tc::bulk_g2s(WT + (c & 1) * WTBUF, hi, (uint32_t)t * 2 * WPART, bar);
+                } else {
+                    tc::bulk_g2s(WT + (c & 1) * WTBUF, hi, (uint32_t)t * WPART, bar);
+                    tc::bulk_g2s(WT + (c & 1) * WTBUF + t * WPART, hi + (size_t)(NB - 1 - g) * WPART, (uint32_t)t * WPART,
+                                 bar);
+                }
                 ++n_wt[c & 1];
             };
             bool ok = true;
@@ -275,9 +301,10 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
 
 size_t trsm_w_bytes(int n) { return wcol_off(n / BLK, n / BLK); }
 
-cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, const char* maps, const float* Z,
-                           ScaleArg sc, float eps, const char* W, int* status, cudaStream_t st) {
-    if (n > MAXNB * BLK || n % BLK) return cudaErrorInvalidValue;
+cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, int j0, int nbp, const float* init,
+                           const char* maps, const float* Z, ScaleArg sc, float eps, const char* W, int* status,
+                           cudaStream_t st) {
+    if (n > 512 || n % BLK || nbp < 1 || nbp > MAXNB || j0 < 0 || (j0 + nbp) * BLK > n) return cudaErrorInvalidValue;
     alignas(64) CUtensorMap zmap;
     memset(&zmap, 0, sizeof(zmap));
     if (Z) {
@@ -286,8 +313,8 @@ cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B
     }
     cudaError_t e = cudaFuncSetAttribute(k_trsm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    k_trsm_tc<<<dim3((K + ROWS - 1) / ROWS, B), NT, SMEM_BYTES, st>>>(p, src, K, n, ldq, maps, zmap, Z ? 1 : 0, sc, eps,
-                                                                    W, status);
+    k_trsm_tc<<<dim3((K + ROWS - 1) / ROWS, B), NT, SMEM_BYTES, st>>>(p, src, K, n, ldq, j0, nbp, init, maps, zmap,
+                                                                    Z ? 1 : 0, sc, eps, W, status);
     return cudaGetLastError();
 }
 

@@ -88,14 +88,16 @@ cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const doubl
 __host__ __device__ inline size_t wcol_off(int nb, int k) { return (size_t)(k * nb - k * (k - 1) / 2) * 2 * 4096; }
 size_t trsm_w_bytes(int n);
 cudaError_t launch_trsm_w(const float* L, const float* Li, int n, int B, char* W, cudaStream_t st);
-// the same solve on the tensor cores from the image W, n <= 256, input rows by the TMA maps (maps: X, 1: Q of matrix
-// b, from launch_tmaps), output to Q; a bounded wait that runs out ORs 0x40 into *status
-cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, const char* maps, const float* Z,
-                           ScaleArg sc, float eps, const char* W, int* status, cudaStream_t st);
-
-// Y = (s X + eps Z) L^-T per matrix: input from `src`, output to Q (in place when src == SRC_Q)
-cudaError_t launch_trsm(PtrArg p, Src src, int K, int n, long long ldx, long long ldq, int B, const float* Z,
-                        ScaleArg sc, float eps, const float* L, const float* Li, cudaStream_t st);
+// the same solve on the tensor cores from the image W, for the panel of blocks j0 .. j0 + nbp - 1 (nbp <= 8) of an
+// n <= 512 matrix; input rows by the TMA maps (launch_tmaps), output to Q; `init` (K x 256 floats per matrix, or
+// null) starts the panel's large accumulators; a bounded wait that runs out ORs 0x40 into *status
+cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, int j0, int nbp, const float* init,
+                           const char* maps, const float* Z, ScaleArg sc, float eps, const char* W, int* status,
+                           cudaStream_t st);
+// scratch[b][row][0 .. 32 nbp) = sum_{k < j0} Y_k W_{j0.., k}^T (Y = the first 32 j0 columns of Q): the second
+// panel's start for launch_trsm_tc; a bounded wait that runs out ORs 0x20 into *status
+cudaError_t launch_trsm_panel_product(PtrArg p, int K, int n, long long ldq, int B, int j0, int nbp, const char* maps,
+                                      const char* W, float* scratch, int* status, cudaStream_t st);
 
 // Q <- Q + Q D per matrix, n <= 512, warp-specialised and fed by TMA (maps from launch_tmaps): D is first split into
 // its operand image `img` (ns_dimg_bytes(n) per matrix); for n > 256 `scratch` holds K x 256 floats per matrix; a

@@ -101,10 +101,10 @@ def trsm_err(Y, X, L, s=1.0, Z=None, eps=0.0):
     return float(np.abs(Y.astype(np.float64) - ex).max() / (np.abs(ex).max() * kappa * U32))
 
 
-@pytest.mark.parametrize("K,n", [(100, 64), (1000, 256), (777, 160), (300, 128), (777, 512)])
+@pytest.mark.parametrize("K,n", [(100, 64), (1000, 256), (777, 160), (300, 128), (777, 512), (600, 352)])
 def test_trsm_forward_error(K, n):
-    """the solve's forward error stays within a few units of kappa(L) u32 of the exact solution, like the oracle's;
-    wider than 256 columns the row-block kernel runs, which reproduces the oracle bit for bit"""
+    """the solve's forward error stays within a few units of kappa(L) u32 of the exact solution, like the oracle's
+    (wider than 256 columns the solve runs as two panels, the second started by the first's product)"""
     rng = np.random.default_rng(K * n)
     X = rng.standard_normal((K, n)).astype(np.float32)
     G, tau = spd(n, 2 * n, K)
@@ -116,5 +116,3 @@ def test_trsm_forward_error(K, n):
     assert e_gpu <= max(4.0, 2 * e_or), (e_gpu, e_or)
     Y2 = gu.trsm(X, L, Li, inplace=True)
     assert trsm_err(Y2, X, L) <= max(4.0, 2 * trsm_err(oracle.trsm(X, L, Li), X, L))
-    if n > 256:
-        assert gu.bits_equal(Y, Yo)

@@ -123,10 +123,11 @@ def _run_local(Xs, Qs):
             continue
         side = _side_streams(dev, NSTREAMS)
         cuts = [len(xs) * i // NSTREAMS for i in range(NSTREAMS + 1)]
+        # The caller's stream waits for every part before this returns, so anything later on it (a free and a reuse
+        # of these tensors' memory included) comes after the parts' work: no record_stream, and the output slab's
+        # memory block is reused call after call.
         for s, a, b in zip(side, cuts[:-1], cuts[1:]):
             s.wait_stream(stream)
-            for t in xs[a:b] + qs[a:b]:
-                t.record_stream(s)   # the caller may drop them before the side stream is done
             _run_group(xs[a:b], qs[a:b], s)
         for s in side:
             stream.wait_stream(s)

@@ -146,6 +146,9 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                         v[h][i] = *reinterpret_cast<const float4*>(raw + h * RAWB + (8 * cw + i) * 512 + 16 * lane);
                 }
             }
+            // the next TMA load into this stage writes through the async proxy: the generic reads above must be
+            // ordered before it by a proxy fence (without it, bytes of chunk c + 2 were seen in place of chunk c's)
+            tc::fence_async_smem();
             tc::mbar_arrive(&bars[B_RAWFREE + st]);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {

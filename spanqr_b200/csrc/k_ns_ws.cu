@@ -148,6 +148,8 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
             float4 v[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const float4*>(raw + 128 * (16 * i + am) + 16 * aq);
+            // the next TMA load into this stage writes through the async proxy: order the generic reads above first
+            tc::fence_async_smem();
             tc::mbar_arrive(&bars[B_RAWFREE + st]);
             if (c >= 2 && !tc::mbar_wait(&bars[B_FREE + st], ring_parity(c - 2))) {   // products of chunk c - 2 done
                 *err = 1;

@@ -278,7 +278,7 @@ def main():
     barrier()
     uuids = [str(torch.cuda.get_device_properties(i).uuid) for i in range(torch.cuda.device_count())]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(uuids) as clk, _lib.KernelTimer() as kt:
+    with ClockSampler(uuids) as clk, _lib.KernelTimer(count_only=True) as kt:
         barrier()
         ev0.record(stream)
         for _ in range(a.steps):
@@ -290,6 +290,20 @@ def main():
     clocks = clk.summary()
     value = B * a.steps / (ms / 1e3)
     gpu_launches = sum(n for _, n in kernels.values())
+
+    # the same steps without the exchange (each rank computes its share only), for the cost of the gather
+    no_gather = None
+    if world > 1:
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        orth_batched(Xs, gather=False)
+        barrier()
+        g0.record(stream)
+        for _ in range(a.steps):
+            orth_batched(Xs, gather=False)
+        g1.record(stream)
+        barrier()
+        gms = dist_max(g0.elapsed_time(g1), device)
+        no_gather = {"value": B * a.steps / (gms / 1e3), "unit": "matrices/s", "ms_per_step": gms / a.steps}
 
     # Per-kernel device times for the roofline: the timed region runs large groups on several streams at once, where
     # one launch's CUDA-event span includes the other streams' work; so the same steps are timed again on one stream
@@ -350,7 +364,8 @@ def main():
             "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": spec["desc"], "batch": B, "partition": "contiguous blocks by cost",
-                       "gather": "NCCL all_gather_into_tensor" if world > 1 else "none (1 GPU)",
+                       "gather": f"NCCL all_gather_into_tensor per wave, {_batched.WAVES} waves overlapped with "
+                                 f"compute" if world > 1 else "none (1 GPU)",
                        "l2": "inputs larger than L2 (352 MB per step for config 3), no flush"},
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_source": src, "traffic": ncu_traffic(dom),
@@ -359,6 +374,7 @@ def main():
                                    f"region (the timed region runs each step in {nstreams} parts on {nstreams} streams)"},
             "kernels_ms_per_step": {k: v[0] / steps_1 for k, v in sorted(kernels.items(), key=lambda kv: -kv[1][0])},
             "gpu_launches": gpu_launches,
+            "without_gather": no_gather,
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,

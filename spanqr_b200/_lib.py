@@ -78,7 +78,10 @@ def workspace_bytes(K, r, batch=1):
 
 class KernelTimer:
     """per-kernel-kind device time of the orth calls made on this thread while active (CUDA events around every
-    launch; see spanqr_timing_enable)"""
+    launch; see spanqr_timing_enable); with count_only=True, launch counts alone (no events on the streams, times 0)"""
+
+    def __init__(self, count_only=False):
+        self.mode = 2 if count_only else 1
 
     def __enter__(self):
         L = lib()
@@ -87,7 +90,7 @@ class KernelTimer:
         self.ms = (ctypes.c_double * self.n)()
         self.launches = (ctypes.c_longlong * self.n)()
         L.spanqr_timing_collect(self.ms, self.launches, 0)   # drop anything pending
-        L.spanqr_timing_enable(1)
+        check(L.spanqr_timing_enable(self.mode), "timing_enable")
         return self
 
     def __exit__(self, *exc):

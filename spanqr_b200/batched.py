@@ -8,7 +8,10 @@ Multi-GPU (torch.distributed initialised, one process per GPU): every rank passe
 matrices are partitioned by cost K * r with a deterministic greedy (largest first, to the least-loaded rank, ties to
 the lower rank); each rank computes its share into its slab of one output buffer laid out owner by owner; then the
 slabs are exchanged over NCCL (all_gather_into_tensor when the slabs are equal, else one broadcast per owner), so every
-rank returns every Q.  With gather=False each rank returns only its own Qs (None elsewhere).
+rank returns every Q.  With gather=False each rank returns only its own Qs (None elsewhere).  For a list input each
+rank computes its share in WAVES waves (consecutive runs of its matrices), the earlier waves on higher-priority streams,
+and the output is laid out wave by wave, owner by owner inside a wave: wave w's exchange, issued on one exchange stream
+in wave order, runs while wave w+1 still computes.
 
 Host-resident matrices (CPU tensors, pinned for the copies to overlap): the batch is cut into chunks, and per chunk the
 copy in, the orth and the copy out run on three streams of the current device with two device buffers in turn, so
@@ -62,6 +65,38 @@ def layout(numels, owner, world):
     return offs, slab, [slab[q + 1] - slab[q] for q in range(world)]
 
 
+def wave_of(owner, world, nwaves):
+    """wave of each matrix: each owner's matrices, in index order, cut in nwaves consecutive runs whose counts differ by
+    at most one (the earlier runs the larger)"""
+    wave = [0] * len(owner)
+    for q in range(world):
+        mine = [i for i, o in enumerate(owner) if o == q]
+        for j, i in enumerate(mine):
+            wave[i] = j * nwaves // len(mine)
+    return wave
+
+
+def wave_layout(numels, owner, world, wave, nwaves):
+    """offsets of each matrix in the flat output laid out wave by wave, owner by owner inside a wave (index order inside
+    one owner's run), and each wave's bounds: owner q's run of wave w is bounds[w][q]..bounds[w][q + 1]"""
+    seg = [[0] * world for _ in range(nwaves)]
+    for i, n in enumerate(numels):
+        seg[wave[i]][owner[i]] += n
+    bounds, off = [], 0
+    for w in range(nwaves):
+        b = [off]
+        for q in range(world):
+            off += seg[w][q]
+            b.append(off)
+        bounds.append(b)
+    pos = [list(b[:world]) for b in bounds]
+    offs = [0] * len(numels)
+    for i, n in enumerate(numels):
+        offs[i] = pos[wave[i]][owner[i]]
+        pos[wave[i]][owner[i]] += n
+    return offs, bounds
+
+
 def exchange(out, slab, sizes, group=None):
     """every rank's slab of `out` to every rank: one all-gather when the slabs are equal, else a broadcast per owner"""
     rank = dist.get_rank(group)
@@ -94,17 +129,31 @@ def _run_group(Xs, Qs, stream):
 
 SPLIT_MIN = 16   # a shape group of at least this many matrices runs as NSTREAMS parts on as many streams
 NSTREAMS = 4
+WAVES = 2        # waves per rank under torch.distributed with gather=True (list inputs)
 _SIDE = {}
 
 
-def _side_streams(dev, n):
-    key = (str(dev), n)
+def _side_streams(dev, n, priority=0):
+    key = (str(dev), n, priority)
     if key not in _SIDE:
-        _SIDE[key] = tuple(torch.cuda.Stream(dev) for _ in range(n))
+        _SIDE[key] = tuple(torch.cuda.Stream(dev, priority=priority) for _ in range(n))
     return _SIDE[key]
 
 
-def _run_local(Xs, Qs):
+def _wave_priority(w, nwaves):
+    """stream priority of wave w: earlier waves higher (more negative), at most three levels above the default; the
+    exchange stream (w = -1) the highest, so the collective's kernels take SMs as soon as its wave is done"""
+    return -3 if w < 0 else -min(nwaves - 1 - w, 3)
+
+
+def _wave_stream(dev, w, nwaves):
+    key = (str(dev), "wave", w, nwaves)
+    if key not in _SIDE:
+        _SIDE[key] = torch.cuda.Stream(dev, priority=_wave_priority(w, nwaves))
+    return _SIDE[key]
+
+
+def _run_local(Xs, Qs, priority=0):
     """orth of a list of matrices on this GPU, one library call per shape.  A large same-shape group is cut in
     NSTREAMS parts that run on as many streams: many kernels leave SMs idle (one Cholesky CTA per matrix, partial last
     waves), and the other parts' kernels fill them.  Each matrix's arithmetic does not depend on the grouping."""
@@ -121,7 +170,7 @@ def _run_local(Xs, Qs):
         if len(xs) < SPLIT_MIN:
             _run_group(xs, qs, stream)
             continue
-        side = _side_streams(dev, NSTREAMS)
+        side = _side_streams(dev, NSTREAMS, priority)
         cuts = [len(xs) * i // NSTREAMS for i in range(NSTREAMS + 1)]
         # The caller's stream waits for every part before this returns, so anything later on it (a free and a reuse
         # of these tensors' memory included) comes after the parts' work: no record_stream, and the output slab's
@@ -241,6 +290,8 @@ def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=8):
     world = dist.get_world_size(group) if distributed else 1
     rank = dist.get_rank(group) if distributed else 0
     owner = partition([x.shape[0] * x.shape[1] for x in Xs], world)
+    if distributed and gather and not stacked and WAVES > 1:
+        return _waves(Xs, owner, world, rank, group, WAVES)
 
     offs, slab, sizes = layout([x.numel() for x in Xs], owner, world)
     with torch.cuda.device(dev):
@@ -255,4 +306,40 @@ def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=8):
     if stacked:
         # equal shapes give a contiguous partition, so the buffer is already in index order
         return out.view(len(Xs), *Xs[0].shape)
+    return Qs
+
+
+def _waves(Xs, owner, world, rank, group, nwaves):
+    """the distributed gather path in waves: wave w of this rank computes on a stream of priority
+    _wave_priority(w, nwaves) (parts on side streams of that priority); its exchange is issued on one exchange stream
+    that waits for that wave only, so the next waves' kernels overlap it.  All exchanges of a call go through that one
+    stream in wave order (a collective issued with async_op=False runs on the current stream, and two collectives of
+    one communicator must not run at once), and every rank issues those of the non-empty waves in the same order."""
+    dev = Xs[0].device
+    wave = wave_of(owner, world, nwaves)
+    offs, bounds = wave_layout([x.numel() for x in Xs], owner, world, wave, nwaves)
+    with torch.cuda.device(dev):
+        cur = torch.cuda.current_stream(dev)
+        out = torch.empty(bounds[-1][world], dtype=torch.float32, device=dev)
+        Qs = [out[offs[i]:offs[i] + Xs[i].numel()].view(Xs[i].shape) for i in range(len(Xs))]
+        for K, r in {tuple(Xs[i].shape) for i in range(len(Xs)) if owner[i] == rank}:
+            zdust(K, r, dev)   # drawn on the caller's stream, which every wave's stream follows
+        xs_stream = _wave_stream(dev, -1, nwaves)
+        xs_stream.wait_stream(cur)
+        used = [xs_stream]
+        for w in range(nwaves):
+            b = bounds[w]
+            if b[world] == b[0]:
+                continue   # empty on every rank: the bounds are the same everywhere
+            s = _wave_stream(dev, w, nwaves)
+            s.wait_stream(cur)
+            with torch.cuda.stream(s):
+                mine = [i for i in range(len(Xs)) if owner[i] == rank and wave[i] == w]
+                _run_local([Xs[i] for i in mine], [Qs[i] for i in mine], _wave_priority(w, nwaves))
+            used.append(s)
+            xs_stream.wait_stream(s)
+            with torch.cuda.stream(xs_stream):
+                exchange(out[b[0]:b[world]], [x - b[0] for x in b], [b[q + 1] - b[q] for q in range(world)], group)
+        for s in used:
+            cur.wait_stream(s)
     return Qs

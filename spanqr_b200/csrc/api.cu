@@ -35,8 +35,9 @@ struct TimedLaunch {
     int kind;
     cudaEvent_t a, b;
 };
-thread_local bool g_timing = false;
+thread_local int g_timing = 0;                    // 0 off, 1 events around every launch, 2 count launches only
 thread_local std::vector<TimedLaunch> g_launches;
+thread_local long long g_counts[K_COUNT] = {};
 thread_local std::vector<cudaEvent_t> g_event_pool;
 
 cudaEvent_t pooled_event() {
@@ -54,6 +55,10 @@ cudaEvent_t pooled_event() {
 template <typename F>
 cudaError_t timed(int kind, cudaStream_t st, F&& launch) {
     if (!g_timing) return launch();
+    if (g_timing == 2) {
+        ++g_counts[kind];
+        return launch();
+    }
     TimedLaunch t{kind, pooled_event(), pooled_event()};
     if (!t.a || !t.b) return launch();
     cudaEventRecord(t.a, st);
@@ -371,8 +376,9 @@ int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* 
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 
-int spanqr_timing_enable(int on) {
-    g_timing = on != 0;
+int spanqr_timing_enable(int mode) {
+    if (mode < 0 || mode > 2) return SPANQR_ERR_ARG;
+    g_timing = mode;
     return SPANQR_OK;
 }
 
@@ -392,6 +398,10 @@ int spanqr_timing_collect(double* ms, long long* launches, int nkinds) {
         g_event_pool.push_back(t.b);
     }
     g_launches.clear();
+    for (int k = 0; k < K_COUNT; ++k) {
+        if (k < nkinds) launches[k] += g_counts[k];
+        g_counts[k] = 0;
+    }
     return rc;
 }
 

@@ -61,6 +61,8 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_gram_f32(al, 64, 32, 64, None, al, al, 10 ** 9, None) == SHAPE           # K < n
     st = ctypes.c_int(7)
     assert L.spanqr_read_status(None, None, ctypes.byref(st)) == ARG
+    assert L.spanqr_timing_enable(3) == ARG and L.spanqr_timing_enable(-1) == ARG
+    assert L.spanqr_timing_enable(2) == OK and L.spanqr_timing_enable(0) == OK
 
 
 def test_error_type_names_the_code():

@@ -7,7 +7,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from spanqr_b200.batched import partition, layout, exchange
+from spanqr_b200.batched import partition, layout, exchange, wave_of, wave_layout
 
 
 def test_partition_equal_costs_is_contiguous_and_balanced():
@@ -33,6 +33,33 @@ def test_layout_owner_major():
     assert offs == [12, 0, 16, 5, 22]
     offs, slab, sizes = layout([4, 4], [0, 0], 3)             # empty slabs
     assert slab == [0, 8, 8, 8] and sizes == [8, 0, 0]
+
+
+def test_wave_of_cuts_each_owner_in_index_order():
+    owner = partition([7] * 13, 3)                            # 5, 4, 4 matrices
+    wave = wave_of(owner, 3, 2)
+    for q in range(3):
+        mine = [wave[i] for i in range(13) if owner[i] == q]
+        assert mine == sorted(mine) and mine.count(0) == -(-len(mine) // 2)
+    assert wave_of([0, 0, 1], 2, 4) == [0, 2, 0]              # fewer matrices than waves
+
+
+@pytest.mark.parametrize("nwaves", [1, 2, 3])
+def test_wave_layout_tiles_the_buffer_wave_then_owner(nwaves):
+    numels = [4, 5, 6, 7, 8, 9, 3, 2]
+    owner = partition(numels, 3)
+    wave = wave_of(owner, 3, nwaves)
+    offs, bounds = wave_layout(numels, owner, 3, wave, nwaves)
+    cells = sorted((offs[i], offs[i] + numels[i]) for i in range(len(numels)))
+    assert cells[0][0] == 0 and cells[-1][1] == sum(numels) == bounds[-1][-1]
+    assert all(a[1] == b[0] for a, b in zip(cells, cells[1:]))              # disjoint and gap-free
+    for w in range(nwaves):
+        assert w == 0 or bounds[w][0] == bounds[w - 1][-1]
+        for q in range(3):
+            run = sorted(i for i in range(len(numels)) if wave[i] == w and owner[i] == q)
+            assert sum(numels[i] for i in run) == bounds[w][q + 1] - bounds[w][q]
+            assert [offs[i] for i in run] == sorted(offs[i] for i in run)   # index order inside a run
+            assert all(bounds[w][q] <= offs[i] < bounds[w][q + 1] for i in run)
 
 
 def _free_port():
@@ -64,6 +91,41 @@ def test_exchange_two_gloo_ranks(sizes):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, 2, port, sizes, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}
+
+
+def _wave_worker(rank, world, port, numels, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        owner = partition(numels, world)
+        wave = wave_of(owner, world, 2)
+        offs, bounds = wave_layout(numels, owner, world, wave, 2)
+        out = torch.full((bounds[-1][world],), -1.0)
+        fill = lambda i: i * 100.0 + torch.arange(numels[i], dtype=torch.float32)
+        for i in range(len(numels)):
+            if owner[i] == rank:
+                out[offs[i]:offs[i] + numels[i]] = fill(i)
+        for b in bounds:
+            if b[world] > b[0]:
+                exchange(out[b[0]:b[world]], [x - b[0] for x in b], [b[p + 1] - b[p] for p in range(world)])
+        q.put((rank, all(torch.equal(out[offs[i]:offs[i] + numels[i]], fill(i)) for i in range(len(numels)))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("numels", [[6] * 8, [6, 9, 4, 4, 7, 3, 5]])
+def test_wave_exchange_two_gloo_ranks(numels):
+    """per-wave exchanges over the wave-major layout leave every rank with every matrix at its offset"""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_wave_worker, args=(r, 2, port, numels, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in procs)

@@ -135,3 +135,17 @@ def test_graph_replay_equals_eager_launches():
         torch.cuda.synchronize()
         for g in got:
             assert gu.bits_equal(g.cpu().numpy(), want.cpu().numpy()), (K, r)
+
+
+def test_kernel_timer_modes_count_the_same_launches():
+    """the event timer and the count-only timer see the same launches of the same kinds; count-only adds no time"""
+    from spanqr_b200 import _lib, orth_batched
+    Xs = [cases.cfg3_matrix(i, K=640).cuda() for i in range(5)]
+    with _lib.KernelTimer() as kt:
+        orth_batched(Xs)
+        timed = kt.collect()
+    with _lib.KernelTimer(count_only=True) as kc:
+        orth_batched(Xs)
+        counted = kc.collect()
+    assert {k: n for k, (_, n) in timed.items()} == {k: n for k, (_, n) in counted.items()}
+    assert all(ms > 0 for ms, _ in timed.values()) and all(ms == 0 for ms, _ in counted.values())

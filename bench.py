@@ -172,9 +172,10 @@ def ncu_traffic(kernel):
 
 def alg_bytes_per_matrix(kind, K, r):
     """algorithmic bytes one launch moves per matrix (the minimum: each input read once, each output written once),
-    averaged over that kind's launches in one orth (k_trsm: pass 1 reads X and Z, passes 2-3 read Y; all write Y)"""
+    averaged over that kind's launches in one orth (k_trsm: every pass reads its input, X or Y, and writes Y; the
+    dust Z of pass 1 is one matrix for the whole batch and is left out)"""
     kr4 = 4.0 * K * r
-    return {"k_absmax": kr4, "k_gram_tc": kr4, "k_gram_tc_acc": kr4, "k_trsm": (3 + 2 + 2) * kr4 / 3.0,
+    return {"k_absmax": kr4, "k_gram_tc": kr4, "k_gram_tc_acc": kr4, "k_trsm": 2 * kr4,
             "k_ns_update": 2 * kr4, "k_gram_reduce": 4.0 * r * r,
             "k_chol": 3 * 4.0 * r * r, "k_trsm_w": 4.0 * r * r, "k_setup": 16.0}.get(kind, 0.0)
 

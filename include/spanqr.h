@@ -126,8 +126,8 @@ int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* 
  * Kernel timing (no reference counterpart; the reference stamps %globaltimer under CHOL_DEBUG, chol.cu:17-23).
  * mode 1: the orth entry points bracket every kernel they launch with CUDA events on the launching stream;
  * mode 2: they only count their launches (no events, nothing added to the streams); mode 0: off.
- * spanqr_timing_collect waits for the events, adds each kernel's duration to ms[kind] and its launches to
- * launches[kind] for kind < nkinds, and forgets them.  Kinds are numbered 0..spanqr_kernel_kinds()-1 (names from
+ * spanqr_timing_collect waits for the events, adds each kind's device time to ms[kind] and its kernel launches to
+ * launches[kind] for kind < nkinds (k_ns_update counts its operand-image kernel too), and forgets them.  Kinds are numbered 0..spanqr_kernel_kinds()-1 (names from
  * spanqr_kernel_kind_name).  Timing state is per host thread.  A mode outside 0..2 returns SPANQR_ERR_ARG.
  */
 int spanqr_timing_enable(int mode);

@@ -34,6 +34,7 @@ const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_
 struct TimedLaunch {
     int kind;
     cudaEvent_t a, b;
+    int nk;   // kernels between the two events
 };
 thread_local int g_timing = 0;                    // 0 off, 1 events around every launch, 2 count launches only
 thread_local std::vector<TimedLaunch> g_launches;
@@ -51,15 +52,15 @@ cudaEvent_t pooled_event() {
     return e;
 }
 
-// run `launch` bracketed by events when timing is on
+// run `launch`, which issues `nk` kernels, bracketed by events (mode 1) or counted (mode 2) when timing is on
 template <typename F>
-cudaError_t timed(int kind, cudaStream_t st, F&& launch) {
+cudaError_t timed(int kind, cudaStream_t st, F&& launch, int nk = 1) {
     if (!g_timing) return launch();
     if (g_timing == 2) {
-        ++g_counts[kind];
+        g_counts[kind] += nk;
         return launch();
     }
-    TimedLaunch t{kind, pooled_event(), pooled_event()};
+    TimedLaunch t{kind, pooled_event(), pooled_event(), nk};
     if (!t.a || !t.b) return launch();
     cudaEventRecord(t.a, st);
     const cudaError_t e = launch();
@@ -190,7 +191,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
         // tensor cores for n <= 256; wider rows keep the shared-memory row-block kernel
         SPQ_TRY(timed(K_NS, st, [&] {
             return launch_ns_ws(p, K, r, ldq, B, G, maps, reinterpret_cast<char*>(P), at<float>(ws, l.nss), status, st);
-        }));
+        }, 2));   // the operand image of D, then the update
     }
 #undef SPQ_TRY
     return SPANQR_OK;
@@ -278,7 +279,7 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
     cudaError_t e = timed(K_SETUP, st, [&] {
         return launch_setup_host(at<MatPtr>(ws, l.ptrs), hX, hQ, batch, at<uint32_t>(ws, l.maxbits),
                                  at<int>(ws, l.status), st);
-    });
+    }, setup_host_launches(batch));
     if (e != cudaSuccess) return cuda_fail(e);
     return run_orth(K, r, batch, r, r, Z, ws, st);
 }
@@ -392,7 +393,7 @@ int spanqr_timing_collect(double* ms, long long* launches, int nkinds) {
         if (e != cudaSuccess) rc = cuda_fail(e);
         else if (t.kind < nkinds) {
             ms[t.kind] += dt;
-            launches[t.kind] += 1;
+            launches[t.kind] += t.nk;
         }
         g_event_pool.push_back(t.a);
         g_event_pool.push_back(t.b);

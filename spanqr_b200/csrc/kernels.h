@@ -36,6 +36,7 @@ cudaError_t launch_setup_strided(MatPtr* tab, const float* X, long long sX, floa
 cudaError_t launch_setup_array(MatPtr* tab, const float* const* dX, float* const* dQ, int B, uint32_t* maxbits,
                                int* status, cudaStream_t st);
 // host arrays of pointers, passed by value to the set-up kernel in chunks
+int setup_host_launches(int B);   // kernels launch_setup_host issues for B pointer pairs
 cudaError_t launch_setup_host(MatPtr* tab, const float* const* hX, float* const* hQ, int B, uint32_t* maxbits,
                               int* status, cudaStream_t st);
 cudaError_t launch_absmax(PtrArg p, int K, int r, long long ldx, int B, uint32_t* maxbits, cudaStream_t st);

@@ -141,6 +141,16 @@ const char* spanqr_kernel_kind_name(int kind);
  */
 int spanqr_read_status(const void* ws, spanqr_stream_t stream, int* device_status);
 
+/*
+ * Self-test of the device timeout path (no reference counterpart; the reference's grid barrier spins without a
+ * limit, candidates/cuk/chol.cu).  Zeroes the status word of `ws` (at least 256 bytes, 256-byte aligned) and
+ * launches one warp that waits on an mbarrier phase for at most limit_ns (1 .. 2e9) nanoseconds; the phase
+ * completes only if `arrive` is non-zero.  A wait that runs out sets bit 0x80 of the status word, read back with
+ * spanqr_read_status (SPANQR_ERR_DEVICE), the same way a production kernel reports its own timeout bit (0x10 Gram,
+ * 0x20 polish update, 0x40 solve).  The kernel returns either way and the context stays usable.
+ */
+int spanqr_selftest_timeout(void* ws, size_t ws_bytes, long long limit_ns, int arrive, spanqr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,6 +24,7 @@ SIGNATURES = {
     "spanqr_read_status": (_I, [_P, _P, ctypes.POINTER(_I)]),
     "spanqr_orth_noalloc_f32": (_I, [_P, _LL, _P, _LL, _I, _I, _P, _P]),
     "spanqr_timing_enable": (_I, [_I]),
+    "spanqr_selftest_timeout": (_I, [_P, _SZ, _LL, _I, _P]),
     "spanqr_timing_collect": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_LL), _I]),
     "spanqr_kernel_kinds": (_I, []),
     "spanqr_kernel_kind_name": (ctypes.c_char_p, [_I]),

@@ -410,6 +410,15 @@ int spanqr_kernel_kinds(void) { return K_COUNT; }
 
 const char* spanqr_kernel_kind_name(int kind) { return (kind >= 0 && kind < K_COUNT) ? KIND_NAMES[kind] : ""; }
 
+int spanqr_selftest_timeout(void* ws, size_t ws_bytes, long long limit_ns, int arrive, spanqr_stream_t stream) {
+    if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0 || ws_bytes < 256) return SPANQR_ERR_WORKSPACE;
+    if (limit_ns <= 0 || limit_ns > 2000000000LL) return SPANQR_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = launch_wait_selftest(arrive != 0, (unsigned long long)limit_ns, static_cast<int*>(ws), st);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
 int spanqr_read_status(const void* ws, spanqr_stream_t stream, int* device_status) {
     if (!ws || !device_status) return SPANQR_ERR_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

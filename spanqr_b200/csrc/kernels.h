@@ -36,6 +36,10 @@ cudaError_t launch_setup_strided(MatPtr* tab, const float* X, long long sX, floa
 cudaError_t launch_setup_array(MatPtr* tab, const float* const* dX, float* const* dQ, int B, uint32_t* maxbits,
                                int* status, cudaStream_t st);
 // host arrays of pointers, passed by value to the set-up kernel in chunks
+// device timeout self-test: one warp waits up to limit_ns on an mbarrier phase that completes only if `arrive`;
+// a wait that runs out ORs SELFTEST_TIMEOUT into *status
+constexpr int SELFTEST_TIMEOUT = 0x80;
+cudaError_t launch_wait_selftest(int arrive, unsigned long long limit_ns, int* status, cudaStream_t st);
 int setup_host_launches(int B);   // kernels launch_setup_host issues for B pointer pairs
 cudaError_t launch_setup_host(MatPtr* tab, const float* const* hX, float* const* hQ, int B, uint32_t* maxbits,
                               int* status, cudaStream_t st);

@@ -63,6 +63,11 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_read_status(None, None, ctypes.byref(st)) == ARG
     assert L.spanqr_timing_enable(3) == ARG and L.spanqr_timing_enable(-1) == ARG
     assert L.spanqr_timing_enable(2) == OK and L.spanqr_timing_enable(0) == OK
+    assert L.spanqr_selftest_timeout(None, 256, 1000, 0, None) == WS
+    assert L.spanqr_selftest_timeout(al + 16, 256, 1000, 0, None) == WS                     # misaligned
+    assert L.spanqr_selftest_timeout(al, 255, 1000, 0, None) == WS                          # too small
+    assert L.spanqr_selftest_timeout(al, 256, 0, 0, None) == ARG                            # no limit
+    assert L.spanqr_selftest_timeout(al, 256, 3 * 10 ** 9, 0, None) == ARG                  # above 2 s
 
 
 def test_error_type_names_the_code():

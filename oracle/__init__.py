@@ -155,6 +155,31 @@ def orth(X, Z, nsm=NSM_B200, eps=EPS, alpha=ALPHA, tau=TAU, ns=NS):
     return Q
 
 
+def borth(X, Z, b=256, nsm=NSM_B200):
+    """candidates/kbig.py:66-95 borth(X, b), reorth on: block Gram-Schmidt (BCGS2) over b-column blocks of
+    s * X (s = pow2_scale(max |x|) of the whole X), each block orthonormalised by orth() with its own slice of the
+    full-width dust Z, projected twice before and once after; projections as float32 GEMMs (numpy)"""
+    X, Z = _c32(X), _c32(Z)
+    K, r = X.shape
+    if r <= b or r % b:
+        return orth(X, Z, nsm=nsm)
+    s = pow2_scale(absmax(X))
+    Q = np.empty_like(X)
+    for j in range(0, r, b):
+        W = X[:, j:j + b] * s
+        Zb = np.ascontiguousarray(Z[:, j:j + b])
+        if j:
+            P = Q[:, :j]
+            W = W - P @ (P.T @ W)
+            W = W - P @ (P.T @ W)
+        W = orth(W, Zb, nsm=nsm)
+        if j:
+            W = W - P @ (P.T @ W)
+            W = orth(W, Zb, nsm=nsm)
+        Q[:, j:j + b] = W
+    return Q
+
+
 def orth_batch(Xs, Zs, nsm=NSM_B200):
     """one orth per matrix, matrices spread over the OpenMP threads (the CPU baseline for orth_batched)"""
     Xs = [_c32(x) for x in Xs]
@@ -186,5 +211,5 @@ def dust(K, r, seed=20261018):
 
 
 __all__ = ["build", "lib", "rsqrt", "pow2_scale", "absmax", "gram_kahan", "gram_plain", "chol32", "trsm",
-           "fro", "ns", "orth", "orth_batch", "num_threads", "dust", "NSM_B200", "EPS", "ALPHA", "TAU", "NS"]
+           "fro", "ns", "orth", "borth", "orth_batch", "num_threads", "dust", "NSM_B200", "EPS", "ALPHA", "TAU", "NS"]
 os.environ.setdefault("OMP_WAIT_POLICY", "PASSIVE")

@@ -77,7 +77,15 @@ def aligned(X):
 def orth(X: torch.Tensor) -> torch.Tensor:
     """Orthonormal basis of the column span of X (fp32 CUDA, K >= r, r a multiple of 32 up to 512).  Where X is
     rank-deficient or zero, the missing directions are completed with arbitrary orthonormal ones (never zero or NaN
-    columns).  Deterministic, no host sync, X left untouched."""
+    columns).  Deterministic, no host sync, X left untouched.  Above r 512 with r a multiple of 256 the columns go
+    through block Gram-Schmidt over 256-column blocks (orth.py:18-19, spanqr_b200.big.borth)."""
+    if torch.is_tensor(X) and X.dim() == 2 and X.shape[1] > MAX_R and X.shape[1] % 256 == 0:
+        if X.dtype != torch.float32 or not X.is_cuda:
+            raise TypeError(f"X must be an fp32 CUDA tensor (got {X.dtype} on {X.device})")
+        if X.shape[0] < X.shape[1]:
+            raise ValueError(f"unsupported shape {X.shape[0]}x{X.shape[1]}: K >= r")
+        from .big import borth
+        return borth(X)
     check_input(X)
     X = aligned(X)
     K, r = X.shape

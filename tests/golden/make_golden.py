@@ -43,14 +43,11 @@ PLAN = [
 ]
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("SPANQR_REF", "/root/reference"))
-    ap.add_argument("--out", default=str(HERE / "golden.npz"))
-    a = ap.parse_args()
-
+def reference_on_cpu(ref):
+    """import the reference from `ref` with the CPU substitutions listed above; returns (torch, triton, gen, kcholqr,
+    kchol, tri, chol32_oracle, trsm_f_interp)"""
     os.environ["TRITON_INTERPRET"] = "1"
-    sys.path.insert(0, a.ref)
+    sys.path.insert(0, ref)
     sys.path.insert(0, str(REPO))
     import torch
 
@@ -83,6 +80,15 @@ def main():
 
     kchol.chol32 = chol32_oracle
     tri.trsm_f = trsm_f_interp
+    return torch, triton, gen, kcholqr, kchol, tri, chol32_oracle, trsm_f_interp
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("SPANQR_REF", "/root/reference"))
+    ap.add_argument("--out", default=str(HERE / "golden.npz"))
+    a = ap.parse_args()
+    torch, triton, gen, kcholqr, kchol, tri, chol32_oracle, trsm_f_interp = reference_on_cpu(a.ref)
 
     out = {}
     names = []

@@ -1,0 +1,47 @@
+"""orth above r 512 (block Gram-Schmidt over 256-column blocks, orth.py:18-19 -> candidates/kbig.py:66-95) on the GPU
+against the oracle's restatement with the same dust: elementwise for kappa <= 1e6, orthogonality, span, bits stable
+from call to call, input untouched."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from spanqr_b200 import orth, zdust
+from tests.test_oracle import _mixed, _kappa, elementwise_tol
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("K,r,kappa,deficient", [(2048, 768, 1e3, False), (5120, 1024, 1e5, False),
+                                                 (2048, 768, 1e3, True)])
+def test_borth_matches_oracle(K, r, kappa, deficient):
+    X = _mixed(K, r, kappa, 11)
+    if deficient:
+        X[:, 512:768] = X[:, :256] @ np.random.default_rng(12).standard_normal((256, 256))
+    X = X.astype(np.float32)
+    Xg = torch.from_numpy(X).cuda()
+    keep = Xg.clone()
+    Q = orth(Xg)
+    Q2 = orth(Xg)
+    torch.cuda.synchronize()
+    assert torch.equal(Xg, keep)
+    assert torch.equal(Q.view(torch.int32), Q2.view(torch.int32))
+    q = Q.cpu().numpy()
+    qo = oracle.borth(X, zdust(K, r, "cuda").cpu().numpy())
+    assert np.isfinite(q).all()
+    qd, qod = q.astype(np.float64), qo.astype(np.float64)
+    err = np.abs(qd.T @ qd - np.eye(r)).max()
+    err_o = np.abs(qod.T @ qod - np.eye(r)).max()
+    assert err <= max(2e-7, 1.5 * err_o), (err, err_o)
+    Xd = X.astype(np.float64)
+    assert np.linalg.norm(Xd - qd @ (qd.T @ Xd)) <= 1e-5 * np.linalg.norm(Xd)
+    if not deficient:
+        assert _kappa(X) <= 1e6
+        assert np.abs(q - qo).max() <= elementwise_tol(_kappa(X))
+
+
+def test_borth_rejects_what_the_block_path_cannot_take():
+    with pytest.raises(ValueError):
+        orth(torch.zeros(2048, 640, device="cuda"))   # r > 512, not a multiple of 256
+    with pytest.raises(ValueError):
+        orth(torch.zeros(700, 768, device="cuda"))    # K < r

@@ -150,3 +150,30 @@ def test_orth_span_within_2x_published_reference():
         w = rows[(K, r, name + "/s0")]
         assert ev["span_n"] <= max(2 * w["span_n"], 1.0), (name, ev["span_n"], w["span_n"])
         assert ev["orth"] <= 2e-7, (name, ev["orth"])
+
+
+def _mixed(K, r, kappa, seed):
+    rng = np.random.default_rng(seed)
+    A = np.linalg.qr(rng.standard_normal((K, r)))[0]
+    B = np.linalg.qr(rng.standard_normal((r, r)))[0]
+    return (A * np.logspace(0, -np.log10(kappa), r)) @ B
+
+
+@pytest.mark.parametrize("deficient", [False, True])
+def test_borth_blocks_are_orth_calls_and_span_x(deficient):
+    """kbig.py:66-95 restated: the first block is orth() of the scaled first block bit for bit; the whole Q is
+    orthonormal and spans X, also when a whole block lies in the span of the first"""
+    K, r = 800, 768
+    X = _mixed(K, r, 1e3, 5)
+    if deficient:
+        X[:, 256:512] = X[:, :256] @ np.random.default_rng(6).standard_normal((256, 256))
+    X = (X * 2.0 ** 7).astype(np.float32)
+    Z = oracle.dust(K, r)
+    Q = oracle.borth(X, Z)
+    s = oracle.pow2_scale(oracle.absmax(X))
+    first = oracle.orth(np.ascontiguousarray(X[:, :256] * s), np.ascontiguousarray(Z[:, :256]))
+    assert np.array_equal(Q[:, :256].view(np.int32), first.view(np.int32))
+    Qd = Q.astype(np.float64)
+    assert np.abs(Qd.T @ Qd - np.eye(r)).max() <= 1e-6
+    Xd = X.astype(np.float64)
+    assert np.linalg.norm(Xd - Qd @ (Qd.T @ Xd)) <= 1e-5 * np.linalg.norm(Xd)

@@ -78,14 +78,26 @@ def orth(X: torch.Tensor) -> torch.Tensor:
     """Orthonormal basis of the column span of X (fp32 CUDA, K >= r, r a multiple of 32 up to 512).  Where X is
     rank-deficient or zero, the missing directions are completed with arbitrary orthonormal ones (never zero or NaN
     columns).  Deterministic, no host sync, X left untouched.  Above r 512 with r a multiple of 256 the columns go
-    through block Gram-Schmidt over 256-column blocks (orth.py:18-19, spanqr_b200.big.borth)."""
-    if torch.is_tensor(X) and X.dim() == 2 and X.shape[1] > MAX_R and X.shape[1] % 256 == 0:
+    through block Gram-Schmidt over 256-column blocks (orth.py:18-19, spanqr_b200.big.borth).  r % 32 != 0 is
+    padded with zero columns to the next multiple of 32 (K must reach it) and the first r columns returned."""
+    if torch.is_tensor(X) and X.dim() == 2 and X.shape[1] > 0 and (X.shape[1] % TB or X.shape[1] > MAX_R):
         if X.dtype != torch.float32 or not X.is_cuda:
             raise TypeError(f"X must be an fp32 CUDA tensor (got {X.dtype} on {X.device})")
-        if X.shape[0] < X.shape[1]:
-            raise ValueError(f"unsupported shape {X.shape[0]}x{X.shape[1]}: K >= r")
-        from .big import borth
-        return borth(X)
+        K, r = X.shape
+        if r % TB:
+            # padded tiles instead of the reference's Householder fallback (kcholqr.py:98-99): zero columns up to
+            # the next multiple of 32 (of 256 above 512); the solve is triangular, so Q's first r columns span X
+            rp = -(-r // TB) * TB if r <= MAX_R else -(-r // 256) * 256
+            if K < rp:
+                raise ValueError(f"unsupported shape {K}x{r}: r % {TB} != 0 needs K >= {rp} (r padded to {rp})")
+            Xp = torch.zeros((K, rp), dtype=torch.float32, device=X.device)
+            Xp[:, :r] = X
+            return orth(Xp)[:, :r].contiguous()
+        if r % 256 == 0:
+            if K < r:
+                raise ValueError(f"unsupported shape {K}x{r}: K >= r")
+            from .big import borth
+            return borth(X)
     check_input(X)
     X = aligned(X)
     K, r = X.shape

@@ -6,8 +6,11 @@ The reference's own ``candidates.kbig.borth(X, 256)`` (kbig.py:66-95; orth.py:18
 256, there) runs with the substitutions of make_golden.py: its Triton kernels under Triton's CPU interpreter, the
 CUDA Cholesky ``kchol.chol32`` replaced by this repo's oracle restatement, the dust drawn on the CPU generator
 (seed 20261018), the projections as torch CPU fp32 GEMMs.  Cases: the reference generator's matrices at 768 x 768
-(three 256-column blocks).  Outputs (float32): X and Q_ref per case.
+(three 256-column blocks), about 13 minutes each.  Outputs per case: the SHA-1 of X (tests/cases.py rebuilds X bit
+for bit), every 8th row of Q_ref (float32; 768 x 768 is the smallest borth shape, and all of Q would not compress),
+and Q_ref's max |Q^T Q - I|.
 """
+import hashlib
 import argparse
 import os
 import sys
@@ -36,10 +39,11 @@ def main():
         X = next(c for c in gen.make_cases(K, r, [name], (0,)) if c.name.split("/")[0] == name).X
         Q = kbig.borth(X, 256)
         key = f"{K}x{r}/{name}"
-        out[f"X/{key}"] = X.numpy().copy()
-        out[f"Q/{key}"] = Q.numpy().copy()
-        names.append(key)
         E = (Q.double().T @ Q.double() - torch.eye(r, dtype=torch.float64)).abs().max()
+        out[f"X_sha1/{key}"] = np.frombuffer(hashlib.sha1(X.numpy().tobytes()).digest(), dtype=np.uint8)
+        out[f"Q_rows8/{key}"] = Q.numpy()[::8].copy()
+        out[f"orth/{key}"] = np.array([float(E)])
+        names.append(key)
         print(f"{key:24s} orth {float(E):.2e}", flush=True)
     out["names"] = np.array(names)
     np.savez_compressed(a.out, **out)

@@ -114,7 +114,7 @@ def test_baseline_configs_quality(name, seed):
 
 def test_rejects_unsupported_shapes_loudly():
     with pytest.raises(ValueError):
-        orth(torch.zeros(100, 48, device="cuda"))
+        orth(torch.zeros(50, 48, device="cuda"))     # r % 32 != 0 pads to 64 > K
     with pytest.raises(TypeError):
         orth(torch.zeros(100, 64, device="cuda", dtype=torch.float64))
 
@@ -149,3 +149,30 @@ def test_kernel_timer_modes_count_the_same_launches():
         counted = kc.collect()
     assert {k: n for k, (_, n) in timed.items()} == {k: n for k, (_, n) in counted.items()}
     assert all(ms > 0 for ms, _ in timed.values()) and all(ms == 0 for ms, _ in counted.values())
+
+
+
+@pytest.mark.parametrize("K,r", [(1000, 100), (3584, 250), (2048, 500)])
+def test_padded_width_not_a_multiple_of_32(K, r):
+    """r % 32 != 0: zero columns up to the next multiple of 32, the first r columns returned; equal to the oracle on
+    the padded matrix, orthonormal, spanning X, and the reference's Householder fallback up to column signs"""
+    from tests.test_oracle import _mixed
+    X = _mixed(K, r, 1e2, 21).astype(np.float32)
+    Q = orth(torch.from_numpy(X).cuda())
+    Q2 = orth(torch.from_numpy(X).cuda())
+    torch.cuda.synchronize()
+    assert Q.shape == (K, r) and torch.equal(Q.view(torch.int32), Q2.view(torch.int32))
+    q = Q.cpu().numpy()
+    rp = -(-r // 32) * 32
+    Xp = np.zeros((K, rp), np.float32)
+    Xp[:, :r] = X
+    qo = oracle.orth(Xp, zdust(K, rp, "cuda").cpu().numpy())[:, :r]
+    tol = elementwise_tol(_kappa(X))
+    assert np.abs(q - qo).max() <= tol
+    qd = q.astype(np.float64)
+    assert np.abs(qd.T @ qd - np.eye(r)).max() <= 2e-7
+    Xd = X.astype(np.float64)
+    assert np.linalg.norm(Xd - qd @ (qd.T @ Xd)) <= 1e-5 * np.linalg.norm(Xd)
+    qh = np.linalg.qr(Xd)[0]
+    qh *= np.sign(np.sum(qh * qd, axis=0))
+    assert np.abs(qd - qh).max() <= tol

@@ -177,3 +177,20 @@ def test_borth_blocks_are_orth_calls_and_span_x(deficient):
     assert np.abs(Qd.T @ Qd - np.eye(r)).max() <= 1e-6
     Xd = X.astype(np.float64)
     assert np.linalg.norm(Xd - Qd @ (Qd.T @ Xd)) <= 1e-5 * np.linalg.norm(Xd)
+
+
+def test_borth_matches_reference_borth_golden():
+    """oracle.borth against the reference's own kbig.borth(X, 256) run on CPU (tests/golden/make_golden_borth.py):
+    the same X (rebuilt by tests/cases.py, checked by hash), the same CPU dust; every 8th row of Q elementwise"""
+    import hashlib
+    g = np.load(GOLD / "golden_borth.npz")
+    assert len(g["names"]) >= 2
+    for key in g["names"]:
+        shape, name = str(key).split("/")
+        K, r = map(int, shape.split("x"))
+        X = cases.make_case(K, r, name).numpy()
+        assert hashlib.sha1(X.tobytes()).digest() == g[f"X_sha1/{key}"].tobytes()
+        Q = oracle.borth(X, oracle.dust(K, r))
+        assert np.abs(Q[::8] - g[f"Q_rows8/{key}"]).max() <= elementwise_tol(_kappa(X)), key
+        Qd = Q.astype(np.float64)
+        assert np.abs(Qd.T @ Qd - np.eye(r)).max() <= max(2e-7, 2 * float(g[f"orth/{key}"][0])), key

@@ -13,9 +13,10 @@ rank computes its share in WAVES waves (consecutive runs of its matrices), the e
 and the output is laid out wave by wave, owner by owner inside a wave: wave w's exchange, issued on one exchange stream
 in wave order, runs while wave w+1 still computes.
 
-Host-resident matrices (CPU tensors, pinned for the copies to overlap): the batch is cut into chunks, and per chunk the
-copy in, the orth and the copy out run on three streams of the current device with two device buffers in turn, so
-the PCIe transfers in both directions overlap each other and the kernels.  Results land in `out` (pinned CPU
+Host-resident matrices (CPU tensors, pinned for the copies to overlap): the batch is cut into chunks (HOST_CHUNKS), and
+per chunk the copy in (one stream), the orth (HOST_COMPUTE streams in turn) and the copy out (one stream) run on the
+current device, through HOST_SLOTS device buffers in turn, so the PCIe transfers in both directions overlap each other
+and the kernels.  Results land in `out` (pinned CPU
 tensors) or in newly allocated pinned tensors; under torch.distributed each rank computes and returns its own share
 (gather=False).
 """

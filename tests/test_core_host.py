@@ -31,3 +31,13 @@ def test_graph_cache_takes_its_lock_without_deadlock(monkeypatch):
     t.join(timeout=10)
     assert done and made == [(64, 32)]
     assert core._graph("cpu", FakeStream(), 64, 32) is done[0]   # cached: built once
+
+
+def test_dispatch_rejects_cpu_tensors_loudly():
+    """the padded (r % 32 != 0) and block (r > 512) branches of orth, like the main path, refuse CPU tensors: there is
+    no CPU path"""
+    import pytest
+    from spanqr_b200 import orth
+    for shape in [(100, 48), (2048, 768), (100, 64)]:
+        with pytest.raises(TypeError):
+            orth(torch.zeros(shape))

@@ -11,7 +11,13 @@ batch (the matrices partitioned over the ranks, results all-gathered over NCCL);
 
 `value` is device time (CUDA events, max over ranks) with inputs resident; `e2e` adds each step's host-to-device copy
 of the rank's inputs (pinned) and device-to-host copy of its results.  `roofline` is the dominant kernel's achieved
-bandwidth (algorithmic bytes / live CUDA-event duration) over the measured HBM copy bandwidth.
+bandwidth (algorithmic bytes per launch / live CUDA-event duration per launch) over the measured HBM copy bandwidth,
+with the whole step's fraction beside it.  On one GPU the line also carries `orth_latency`: orth() microseconds per
+call at the eight TTF shapes (isolated calls with L2 flushed, and back-to-back bursts, as the reference's
+qrbench/bench.py:28-53 times them), with cuSOLVER Householder (torch.linalg.qr) on the same GPU beside each.
+`cpu_baseline` (and `--impl reference`) time the reference's pure-PyTorch CPU path (rcholqr, restated in
+oracle/rcholqr.py) on the host cores, with LAPACK Householder (torch.linalg.qr) and the C restatement of the GPU
+recipe (oracle/spanqr_oracle.c) beside it.
 """
 import argparse
 import json
@@ -43,6 +49,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (tests / profiling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-latency", action="store_true", help="skip the per-shape orth() latency block")
     return ap.parse_args()
 
 
@@ -170,14 +177,23 @@ def ncu_traffic(kernel):
     return None
 
 
-def alg_bytes_per_matrix(kind, K, r):
-    """algorithmic bytes one launch moves per matrix (the minimum: each input read once, each output written once),
-    averaged over that kind's launches in one orth (k_trsm: every pass reads its input, X or Y, and writes Y; the
-    dust Z of pass 1 is one matrix for the whole batch and is left out)"""
+def alg_bytes_per_call(kind, K, r):
+    """algorithmic bytes of one orth call of one K x r matrix spent in the launches of one kernel kind (each input
+    read once, each output written once): k_trsm: three passes, each reading its input (X or Y) and writing Y (the
+    dust Z of pass 1 is one matrix shared by the batch and left out); k_gram_tc: the Grams of passes 1-3 and of the
+    first polish step, each reading Y once; k_gram_tc_acc: the last polish step's Gram; k_ns_update: two polish
+    updates, each reading and writing Y; k_absmax: one read of X.  Divided by that kind's launches per call it gives
+    the bytes per launch and matrix."""
     kr4 = 4.0 * K * r
-    return {"k_absmax": kr4, "k_gram_tc": kr4, "k_gram_tc_acc": kr4, "k_trsm": 2 * kr4,
-            "k_ns_update": 2 * kr4, "k_gram_reduce": 4.0 * r * r,
-            "k_chol": 3 * 4.0 * r * r, "k_trsm_w": 4.0 * r * r, "k_setup": 16.0}.get(kind, 0.0)
+    return {"k_absmax": kr4, "k_gram_tc": 4 * kr4, "k_gram_tc_acc": kr4, "k_trsm": 3 * 2 * kr4,
+            "k_ns_update": 2 * 2 * kr4, "k_gram_reduce": 5 * 4.0 * r * r,
+            "k_chol": 3 * 3 * 4.0 * r * r, "k_trsm_w": 3 * 4.0 * r * r, "k_setup": 16.0}.get(kind, 0.0)
+
+
+def alg_bytes_orth(K, r):
+    """the whole orth call's algorithmic bytes, 17 reads or writes of a K x r fp32 matrix (absmax 1, Grams 5, the
+    three solves 2 each, the two polish updates 2 each)"""
+    return 17 * 4.0 * K * r
 
 
 def dist_max(x, device):
@@ -191,59 +207,142 @@ def dist_max(x, device):
 # ---------------------------------------------------------------------------------------------------------------
 # arms
 
-def _host_sample(K, r, th):
-    """one config-3 member per OpenMP thread (at most 64 distinct matrices, reused beyond that)"""
+def _host_sample(K, r, n):
+    """n config-3 members (at most 64 distinct matrices, reused beyond that), fp32 CPU tensors"""
     from tests import cases
-    distinct = [cases.cfg3_matrix(i, K, r).numpy() for i in range(min(th, 64))]
-    return [distinct[i % len(distinct)] for i in range(th)]
+    distinct = [cases.cfg3_matrix(i, K, r) for i in range(min(n, 64))]
+    return [distinct[i % len(distinct)] for i in range(n)]
 
 
-def cpu_baseline(spec, budget_s=20.0):
-    """the oracle (a C restatement of the reference's kcholqr_f) on this host's cores, one matrix per thread, for
-    about `budget_s` seconds"""
+def _time_cpu(fn, xs, budget_s):
+    """matrices/s of fn over the sample xs, one warm-up call, then whole passes over xs for about budget_s seconds"""
+    fn(xs[0])
+    t = time.perf_counter()
+    n = 0
+    while True:
+        for x in xs:
+            fn(x)
+        n += len(xs)
+        dt = time.perf_counter() - t
+        if dt >= budget_s:
+            return n / dt, n, dt
+
+
+def cpu_baselines(K, r, budget_s=8.0):
+    """The reference's CPU path on this host's cores, on config-3 members: its pure-PyTorch rcholqr (the value), LAPACK
+    Householder torch.linalg.qr and the C restatement of the GPU recipe kcholqr_f (one matrix per OpenMP thread)."""
     import oracle
-    K, r = spec["shapes"][0]
-    th = oracle.num_threads()
+    from oracle.rcholqr import rcholqr
+    th = os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(th)
+    try:
+        xs = _host_sample(K, r, 8)
+        v_rc, n_rc, t_rc = _time_cpu(rcholqr, xs, budget_s)
+        v_hh, n_hh, t_hh = _time_cpu(lambda x: torch.linalg.qr(x)[0], xs, budget_s / 2)
+    finally:
+        torch.set_num_threads(prev)
+    oth = oracle.num_threads()
     Z = oracle.dust(K, r)
-    Xs = _host_sample(K, r, th)
+    Xo = [x.numpy() for x in _host_sample(K, r, oth)]
     t = time.perf_counter()
-    oracle.orth_batch(Xs, [Z] * th)
-    one = time.perf_counter() - t
-    rounds = int(min(32, max(1, budget_s / max(one, 1e-3))))
-    t = time.perf_counter()
-    for _ in range(rounds):
-        oracle.orth_batch(Xs, [Z] * th)
-    dt = time.perf_counter() - t
-    return {"value": rounds * th / dt, "unit": "matrices/s", "cores": th, "kind": "port",
-            "sample": f"{rounds} x {th} matrices of {K}x{r} (config-3 members), one per OpenMP thread, {dt:.1f} s"}
+    oracle.orth_batch(Xo, [Z] * oth)
+    t_or = time.perf_counter() - t
+    return {"value": v_rc, "unit": "matrices/s", "cores": th, "kind": "port",
+            "sample": f"rcholqr (reference candidates/rcholqr.py:61-65, restated in oracle/rcholqr.py) on {n_rc} "
+                      f"config-3 members of {K}x{r} (8 distinct), torch CPU on {th} threads, {t_rc:.1f} s",
+            "householder_cpu": {"value": v_hh, "unit": "matrices/s", "cores": th,
+                                "sample": f"torch.linalg.qr(X)[0] (LAPACK) on {n_hh} of the same matrices, {t_hh:.1f} s"},
+            "kcholqr_f_port": {"value": oth / t_or, "unit": "matrices/s", "cores": oth,
+                               "sample": f"the C restatement of kcholqr_f (oracle/spanqr_oracle.c) on {oth} matrices, "
+                                         f"one per OpenMP thread, {t_or:.1f} s"}}
 
 
 def run_reference(a, spec):
-    """--impl reference: the reference's CPU path (the oracle port of kcholqr_f) on the host cores"""
+    """--impl reference: the reference's CPU path on the host cores -- its pure-PyTorch rcholqr (restated in
+    oracle/rcholqr.py; the reference's GPU path needs Triton and NVRTC on a GPU and has no CPU form), torch on every
+    host thread, one step = one pass over a sample of config-3 members; LAPACK Householder timed beside it"""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import oracle
+    from oracle.rcholqr import rcholqr
     K, r = spec["shapes"][0]
-    th = oracle.num_threads()
-    Z = oracle.dust(K, r)
-    Xs = _host_sample(K, r, th)
+    th = os.cpu_count() or 1
+    torch.set_num_threads(th)
+    xs = _host_sample(K, r, 8)
     for _ in range(a.warmup):
-        oracle.orth_batch(Xs, [Z] * th)
+        for x in xs:
+            rcholqr(x)
     t = time.perf_counter()
     for _ in range(a.steps):
-        oracle.orth_batch(Xs, [Z] * len(Xs))
+        for x in xs:
+            rcholqr(x)
     dt = time.perf_counter() - t
-    v = len(Xs) * a.steps / dt
+    v = len(xs) * a.steps / dt
+    v_hh, n_hh, t_hh = _time_cpu(lambda x: torch.linalg.qr(x)[0], xs, 4.0)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "matrices/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * dt / a.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": spec["desc"] + f"; host sample of {len(Xs)} matrices per step"},
+            "config": {"workload": spec["desc"] + f"; each step a host sample of {len(xs)} of its matrices"},
             "cpu_baseline": {"value": v, "unit": "matrices/s", "cores": th, "kind": "port",
-                             "sample": f"{len(Xs)} matrices of {K}x{r} per step, one per OpenMP thread"},
+                             "sample": f"rcholqr (reference candidates/rcholqr.py:61-65, restated in oracle/rcholqr.py)"
+                                       f", {len(xs)} config-3 members of {K}x{r} per step, torch CPU on {th} threads",
+                             "householder_cpu": {"value": v_hh, "unit": "matrices/s", "cores": th,
+                                                 "sample": f"torch.linalg.qr(X)[0] on {n_hh} of the same matrices"}},
             "e2e": {"value": v, "unit": "matrices/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+TTF_SHAPES = [(768, 512), (2048, 512), (1024, 256), (2048, 256), (3584, 256), (5120, 256), (6144, 256), (17408, 256)]
+
+
+def _time_calls(fn, X, flush, reps=20, bursts=5, burst=20):
+    """(lat, thr) in microseconds, medians of CUDA-event times as the reference's qrbench/bench.py:28-53 takes them:
+    lat = one call, synchronised before and after, L2 flushed before each (a write of 2x L2); thr = a burst of calls
+    back to back, per call"""
+    for _ in range(5):
+        fn(X)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lat = []
+    for _ in range(reps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        s.record()
+        fn(X)
+        e.record()
+        torch.cuda.synchronize()
+        lat.append(s.elapsed_time(e) * 1e3)
+    thr = []
+    for _ in range(bursts):
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(burst):
+            fn(X)
+        e.record()
+        torch.cuda.synchronize()
+        thr.append(s.elapsed_time(e) * 1e3 / burst)
+    return statistics.median(lat), statistics.median(thr)
+
+
+def orth_latency(device, hbm):
+    """orth() per call at the TTF shapes on the reference bench's default case (ttf_cu4_t1e-2), with cuSOLVER
+    Householder (torch.linalg.qr, the reference's "householder" method, qrbench/methods.py) on the same GPU"""
+    from spanqr_b200 import orth
+    from tests import cases
+    flush = torch.empty(2 * 126 * 2 ** 20, dtype=torch.uint8, device=device)
+    rows = []
+    for K, r in TTF_SHAPES:
+        X = cases.make_case(K, r, "ttf_cu4_t1e-2").to(device)
+        lat, thr = _time_calls(orth, X, flush)
+        hl, ht = _time_calls(lambda x: torch.linalg.qr(x)[0], X, flush)
+        rows.append({"shape": f"{K}x{r}", "lat_us": round(lat, 1), "thr_us": round(thr, 1),
+                     "householder_lat_us": round(hl, 1), "householder_thr_us": round(ht, 1),
+                     "speedup_lat": round(hl / lat, 2), "speedup_thr": round(ht / thr, 2),
+                     "hbm_frac_lat": round(alg_bytes_orth(K, r) / (lat * 1e-6) / 1e9 / hbm, 4)})
+    del flush
+    return rows
 
 
 def main():
@@ -322,16 +421,19 @@ def main():
         _batched.NSTREAMS = nstreams
     steps_1 = a.steps
 
-    # dominant kernel and its roofline (this rank's launches; per-rank work is balanced)
+    # dominant kernel and its roofline (this rank's launches; per-rank work is balanced): the kind's algorithmic bytes
+    # per call, summed over this rank's matrices, divided by the kind's launches per step (each launch covers all of
+    # them on the one-stream pass)
     hbm, bf16, src = peaks()
     dom = max(kernels.items(), key=lambda kv: kv[1][0])[0]
     dom_ms, dom_n = kernels[dom]
     owner = partition([K * r for K, r in spec["shapes"]], world)
     mine = [spec["shapes"][i] for i in range(B) if owner[i] == rank]
-    per_step_bytes = sum(alg_bytes_per_matrix(dom, K, r) for K, r in mine)
     launches_per_step = dom_n / steps_1
-    bytes_per_launch = per_step_bytes / max(launches_per_step, 1)
+    bytes_per_launch = sum(alg_bytes_per_call(dom, K, r) for K, r in mine) / max(launches_per_step, 1)
     achieved = bytes_per_launch / (dom_ms / dom_n / 1e3) / 1e9
+    step_bytes = sum(alg_bytes_orth(K, r) for K, r in mine)
+    step_gbs = step_bytes / (ms / a.steps / 1e3) / 1e9
 
     # end to end through the public API: pinned host inputs of this rank's share in, its results out
     e2e = None
@@ -355,9 +457,13 @@ def main():
         e2e = {"value": B * a.steps / (ems / 1e3), "unit": "matrices/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": h2d, "ms_per_step": ems / a.steps}
 
+    lat_rows = None
+    if world == 1 and not a.no_latency:
+        lat_rows = orth_latency(device, hbm)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        cpu = cpu_baseline(spec)
+        cpu = cpu_baselines(*spec["shapes"][0])
 
     if rank == 0:
         line = {
@@ -371,6 +477,9 @@ def main():
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_source": src, "traffic": ncu_traffic(dom),
                          "alg_bytes_per_launch": bytes_per_launch, "avg_launch_ms": dom_ms / dom_n,
+                         "launches_per_step": launches_per_step,
+                         "step": {"alg_bytes": step_bytes, "achieved": step_gbs, "frac": step_gbs / hbm,
+                                  "what": "17 reads/writes of every K x r matrix per orth over the timed step"},
                          "timing": f"CUDA events around every launch, {steps_1} steps on one stream after the timed "
                                    f"region (the timed region runs each step in {nstreams} parts on {nstreams} streams)"},
             "kernels_ms_per_step": {k: v[0] / steps_1 for k, v in sorted(kernels.items(), key=lambda kv: -kv[1][0])},
@@ -379,6 +488,7 @@ def main():
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "orth_latency": lat_rows,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -20,6 +20,7 @@
  *   spanqr_orth_batched_f32  no reference counterpart: same, from device arrays of matrix pointers
  *   spanqr_orth_ptrs_f32     no reference counterpart: same, from host arrays of matrix pointers
  *   spanqr_gram_f32          candidates/tri.py:362-375 gram_f(Y, s) and tri.py:285-297 gram_split(Y, bt=64)
+ *   spanqr_gram_mode_f32     the same, and kcholqr.py:106 Y.T @ Y (each Gram of the orth sequence on its own)
  *   spanqr_chol_f32          candidates/kchol.py:35-44 chol32(G, tau) (kernel candidates/cuk/chol.cu:273-276)
  *   spanqr_trsm_f32          candidates/tri.py:406-412 trsm_f(X, L, Li, s, Z, eps)
  */
@@ -89,11 +90,20 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
  * SPANQR_ERR_TOO_LARGE.  The first call on each device looks up the array's device address (cudaGetSymbolAddress,
  * with that device current), so make that first call before any stream capture.  All calls share the one array:
  * calls that overlap on the GPU (other streams or threads) race and corrupt each other's results; serialise them.
- * Nothing is allocated or freed, by this library or by any library it calls.
+ * Nothing is allocated or freed, by this library or by any library it calls.  The device address is cached per
+ * device and per context: after a cudaDeviceReset the next call looks it up again (do that call outside a capture).
  */
 #define SPANQR_NOALLOC_SCRATCH_BYTES (16u << 20)
 int spanqr_orth_noalloc_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z,
                             spanqr_stream_t stream);
+
+/*
+ * The device status word of spanqr_orth_noalloc_f32's scratch array on the current device (the counterpart of
+ * spanqr_read_status for that entry point, whose scratch the caller cannot address): 0 = the last no-allocation call
+ * recorded no failure; otherwise its bounded device waits ran out and Q must not be used (SPANQR_ERR_DEVICE).  No
+ * reference counterpart.  Synchronises `stream`; allocates nothing.
+ */
+int spanqr_noalloc_read_status(spanqr_stream_t stream, int* device_status);
 
 /*
  * Component entry points (the reference's kernel modules), for tests and for callers that compose their own
@@ -105,6 +115,17 @@ int spanqr_orth_noalloc_f32(const float* X, long long ldx, float* Q, long long l
  */
 int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_s, float* G, void* ws,
                     size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * spanqr_gram_mode_f32: the same G with the arithmetic of one of the orth sequence's Grams, so that each can be
+ *   checked on its own: SPANQR_GRAM_ACCURATE (= spanqr_gram_f32), SPANQR_GRAM_PASS (the Gram of every Cholesky-QR
+ *   pass and of the first polish step: the reference's gram_f in pass 1, tri.py:362-375, and its plain SGEMM
+ *   Y.T @ Y, kcholqr.py:106), SPANQR_GRAM_POLISH (the last polish step's Gram: the reference's gram_split,
+ *   kcholqr.py:20, tri.py:285-297).  Any other mode returns SPANQR_ERR_ARG.
+ */
+enum spanqr_gram_mode { SPANQR_GRAM_ACCURATE = 0, SPANQR_GRAM_PASS = 1, SPANQR_GRAM_POLISH = 2 };
+int spanqr_gram_mode_f32(const float* Y, long long ldy, int K, int n, const float* d_s, int mode, float* G, void* ws,
+                         size_t ws_bytes, spanqr_stream_t stream);
 
 /*
  * spanqr_chol_f32: lower Cholesky factor of G [n, n] (lower triangle read, G left unchanged) with every pivot

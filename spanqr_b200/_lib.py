@@ -23,6 +23,8 @@ SIGNATURES = {
     "spanqr_trsm_f32": (_I, [_P, _LL, _P, _P, _F, _P, _P, _I, _I, _P, _LL, _P, _SZ, _P]),
     "spanqr_read_status": (_I, [_P, _P, ctypes.POINTER(_I)]),
     "spanqr_orth_noalloc_f32": (_I, [_P, _LL, _P, _LL, _I, _I, _P, _P]),
+    "spanqr_noalloc_read_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "spanqr_gram_mode_f32": (_I, [_P, _LL, _I, _I, _P, _I, _P, _P, _SZ, _P]),
     "spanqr_timing_enable": (_I, [_I]),
     "spanqr_selftest_timeout": (_I, [_P, _SZ, _LL, _I, _P]),
     "spanqr_timing_collect": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_LL), _I]),

@@ -290,12 +290,49 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
 // For callers that may not call cudaMalloc (inside a stream capture that must not add allocations, in a
 // memory-capped sandbox, in a real-time loop).  The array belongs to the library's module: each GPU that loads the
 // library keeps it until the process exits.  Its host-side name is only a stand-in, never a device address; the
-// device address is looked up once per device with cudaGetSymbolAddress and cached.
+// device address is looked up with cudaGetSymbolAddress once per device and context (a cudaDeviceReset gives the
+// device a new context, and with it a new copy of the array, so the cached address is keyed on the context too).
 namespace {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[SPANQR_NOALLOC_SCRATCH_BYTES];
 constexpr int NOALLOC_MAX_DEVICES = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+struct NoallocSlot {
+    void* ctx;
+    void* ptr;
+};
+NoallocSlot g_noalloc[NOALLOC_MAX_DEVICES] = {};
+
+using CtxGetCurrentFn = int (*)(void**);   // cuCtxGetCurrent(CUcontext*)
+CtxGetCurrentFn g_ctx_get = nullptr;
+std::once_flag g_ctx_once;
+
+// the scratch array's device address for the current device and context (looked up on first use)
+int noalloc_scratch(void** out) {
+    std::call_once(g_ctx_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_get = reinterpret_cast<CtxGetCurrentFn>(fn);
+    });
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return SPANQR_ERR_ARG;
+    void* ctx = nullptr;
+    if (!g_ctx_get || g_ctx_get(&ctx) != 0) return cuda_fail(cudaErrorNotSupported);
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!ctx || !g_noalloc[dev].ptr || g_noalloc[dev].ctx != ctx) {
+        // with device `dev` current; the lookup also makes the device's primary context current if none was
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e);
+        if (g_ctx_get(&ctx) != 0 || !ctx) return cuda_fail(cudaErrorNotSupported);
+        g_noalloc[dev] = NoallocSlot{ctx, p};
+    }
+    *out = g_noalloc[dev].ptr;
+    return SPANQR_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -305,24 +342,19 @@ int spanqr_orth_noalloc_f32(const float* X, long long ldx, float* Q, long long l
     int rc = check_shape(K, r, 1);
     if (rc) return rc;
     if (layout(K, r, 1).total > SPANQR_NOALLOC_SCRATCH_BYTES) return SPANQR_ERR_TOO_LARGE;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_fail(e);
-    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return SPANQR_ERR_ARG;
     void* scratch = nullptr;
-    {
-        std::lock_guard<std::mutex> g(g_noalloc_mu);
-        if (!g_noalloc_ptr[dev]) {
-            void* p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // with device `dev` current
-            if (e != cudaSuccess) return cuda_fail(e);
-            g_noalloc_ptr[dev] = p;
-        }
-        scratch = g_noalloc_ptr[dev];
-    }
+    if ((rc = noalloc_scratch(&scratch))) return rc;
     // the set-up kernel of the orth sequence clears the only scratch words that must start at zero (the per-matrix
     // max |x| bits and the status word); every other scratch region is fully written before it is read
     return spanqr_orth_f32(X, ldx, Q, ldq, K, r, Z, scratch, SPANQR_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+int spanqr_noalloc_read_status(spanqr_stream_t stream, int* device_status) {
+    if (!device_status) return SPANQR_ERR_ARG;
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    return spanqr_read_status(scratch, stream, device_status);   // the status word leads the scratch layout
 }
 
 int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_s, float* G, void* ws,
@@ -340,6 +372,35 @@ int spanqr_gram_f32(const float* Y, long long ldy, int K, int n, const float* d_
         e = launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, ScaleArg{nullptr, d_s}, GRAM_ACCURATE, at<float>(ws, l.P),
                            at<int>(ws, l.status), st);
     if (e == cudaSuccess) e = launch_gram_reduce(at<float>(ws, l.P), n, 1, gp, 0, G, nullptr, st);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_gram_mode_f32(const float* Y, long long ldy, int K, int n, const float* d_s, int mode, float* G, void* ws,
+                         size_t ws_bytes, spanqr_stream_t stream) {
+    if (mode == SPANQR_GRAM_ACCURATE) return spanqr_gram_f32(Y, ldy, K, n, d_s, G, ws, ws_bytes, stream);
+    if (mode != SPANQR_GRAM_PASS && mode != SPANQR_GRAM_POLISH) return SPANQR_ERR_ARG;
+    int rc = check_shape(K, n, 1);
+    if (rc) return rc;
+    if (!Y || !G || !a16(Y) || ldy < n || ldy % 4) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, n, 1))) return rc;
+    const Layout l = layout(K, n, 1);
+    const GramPlan gp = gram_tc_plan(K, n);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    PtrArg p{nullptr, MatPtr{Y, const_cast<float*>(Y)}};
+    const ScaleArg sc{nullptr, d_s};
+    int* status = at<int>(ws, l.status);
+    float* P = at<float>(ws, l.P);
+    cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), st);
+    if (e == cudaSuccess && mode == SPANQR_GRAM_PASS && n <= 256)
+        e = launch_tmaps(p, K, n, ldy, ldy, 1, ws, at<char>(ws, l.maps), st);
+    if (e == cudaSuccess) {
+        if (mode == SPANQR_GRAM_PASS)   // the Gram of every Cholesky-QR pass and of the first polish step
+            e = n <= 256 ? launch_gram_ws(p, SRC_X, K, n, 1, gp, at<char>(ws, l.maps), sc, P, status, st)
+                         : launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, sc, GRAM_PLAIN, P, status, st);
+        else   // the last polish step's Gram
+            e = launch_gram_tc(p, SRC_X, K, n, ldy, 1, gp, sc, GRAM_DRAINED, P, status, st);
+    }
+    if (e == cudaSuccess) e = launch_gram_reduce(P, n, 1, gp, 0, G, nullptr, st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 

@@ -12,8 +12,10 @@
 // against the large partial sum.  After every group of rows the large-term accumulator is drained into fp64 registers
 // while the next group accumulates in the other TMEM buffer; the small-term accumulator (about 2^-11 of the total) stays in
 // TMEM for the whole split and is drained once at the end.  The split's fp64 sum is rounded to fp32 and written as
-// a partial.  k_gram_reduce (k_gram.cu) sums the partials in split order in fp64.  The accurate mode serves the two
-// Grams the reference computes with its compensated kernel (pass 1 and the last polish step, kcholqr.py:20, 106).
+// a partial.  k_gram_reduce (k_gram.cu) sums the partials in split order in fp64.  Which mode runs where: the orth
+// sequence uses the drained mode for its last polish Gram (the reference's compensated gram_split, kcholqr.py:20) and
+// the plain mode for the Grams of r > 256 (k_gram_ws covers r <= 256); the accurate mode serves the component entry
+// point spanqr_gram_f32, the counterpart of the reference's compensated gram_f / gram_split (tri.py:285-375).
 // Determinism: the split size (512 rows) and every order depend only on (K, n), never on the batch or the GPU.
 // Compensation: the reference (candidates/tri.py:255-375) Kahan-sums fp32 32-row dots inside a split and adds the
 // splits in fp64; here each group of rows (32 in the accurate mode, 128 in the plain mode) sums its products in the

@@ -85,9 +85,12 @@ def reference_on_cpu(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("SPANQR_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("SPANQR_REF"),
+                    help="checkout of oguzeldereli/spanqr (or set SPANQR_REF)")
     ap.add_argument("--out", default=str(HERE / "golden.npz"))
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference checkout with --ref or SPANQR_REF")
     torch, triton, gen, kcholqr, kchol, tri, chol32_oracle, trsm_f_interp = reference_on_cpu(a.ref)
 
     out = {}

@@ -27,10 +27,13 @@ CASES = [(768, 768, "mixed_c2"), (768, 768, "mixed_c4")]
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("SPANQR_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("SPANQR_REF"),
+                    help="checkout of oguzeldereli/spanqr (or set SPANQR_REF)")
     ap.add_argument("--out", default=str(HERE / "golden_borth.npz"))
     ap.add_argument("--cases", type=int, default=len(CASES))
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("give the reference checkout with --ref or SPANQR_REF")
     torch, triton, gen, kcholqr, kchol, tri, _, _ = reference_on_cpu(a.ref)
     from candidates import kbig
     out = {}

@@ -59,8 +59,12 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_chol_f32(al, 100, al, al, al, al, 10 ** 9, None) == SHAPE
     assert L.spanqr_trsm_f32(al, 64, None, None, 0.0, al, al, 256, 64, al, 60, al, 10 ** 9, None) == ARG
     assert L.spanqr_gram_f32(al, 64, 32, 64, None, al, al, 10 ** 9, None) == SHAPE           # K < n
+    assert L.spanqr_gram_mode_f32(al, 64, 256, 64, None, 3, al, al, 10 ** 9, None) == ARG      # no such mode
+    assert L.spanqr_gram_mode_f32(al, 64, 32, 64, None, 1, al, al, 10 ** 9, None) == SHAPE     # K < n
+    assert L.spanqr_gram_mode_f32(al, 64, 256, 64, None, 2, al, al, ws_need - 1, None) == WS   # workspace too small
     st = ctypes.c_int(7)
     assert L.spanqr_read_status(None, None, ctypes.byref(st)) == ARG
+    assert L.spanqr_noalloc_read_status(None, None) == ARG
     assert L.spanqr_timing_enable(3) == ARG and L.spanqr_timing_enable(-1) == ARG
     assert L.spanqr_timing_enable(2) == OK and L.spanqr_timing_enable(0) == OK
     assert L.spanqr_selftest_timeout(None, 256, 1000, 0, None) == WS

@@ -27,7 +27,7 @@ def spd(n, K, seed, shift_rel=1e-7):
     return G, np.float32(np.float32(np.float32(1e-8) * nrm) + np.float32(1e-30))
 
 
-@pytest.mark.parametrize("n", [32, 64, 96, 128, 256, 512])
+@pytest.mark.parametrize("n", [32, 64, 96, 128, 160, 256, 288, 480, 512])
 def test_chol_bitwise(n):
     G, tau = spd(n, 3 * n, n)
     L, Li = gu.chol(G, tau)

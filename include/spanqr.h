@@ -19,6 +19,7 @@
  *   spanqr_orth_strided_f32  no reference counterpart: a batch of same-shape layers (orth_batched)
  *   spanqr_orth_batched_f32  no reference counterpart: same, from device arrays of matrix pointers
  *   spanqr_orth_ptrs_f32     no reference counterpart: same, from host arrays of matrix pointers
+ *   spanqr_orth_graph_*      no reference counterpart: spanqr_orth_f32 captured once per shape, replayed per call
  *   spanqr_gram_f32          candidates/tri.py:362-375 gram_f(Y, s) and tri.py:285-297 gram_split(Y, bt=64)
  *   spanqr_gram_mode_f32     the same, and kcholqr.py:106 Y.T @ Y (each Gram of the orth sequence on its own)
  *   spanqr_chol_f32          candidates/kchol.py:35-44 chol32(G, tau) (kernel candidates/cuk/chol.cu:273-276)
@@ -80,6 +81,24 @@ int spanqr_orth_batched_f32(const float* const* dX, float* const* dQ, int K, int
  * host-to-device copy and no pinned memory is involved; leading dimension r for all) */
 int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r, int batch, const float* Z,
                          void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * orth of one shape as one CUDA graph (no reference counterpart; the reference launches kernel by kernel from Python,
+ * candidates/kcholqr.py:92-112).  spanqr_orth_graph_create captures the whole kernel sequence of spanqr_orth_f32 for
+ * shape K x r with leading dimensions ldx, ldq, the dust Z and the workspace ws (all baked into the graph; Z and ws must
+ * stay valid and unchanged until the graph is destroyed) and instantiates it, on the current device, from outside any
+ * stream capture; it enqueues nothing.  spanqr_orth_graph_launch replays it for Q = orth(X) on `stream`: only the
+ * set-up kernel's X and Q arguments are replaced, so no copy of X or Q is made and every later kernel is launched as
+ * captured; the bits equal spanqr_orth_f32's.  Launches of one graph share its workspace: issue them from one host
+ * thread and keep them ordered on one stream (or serialise them), as with calls sharing a workspace.  The launch
+ * returns SPANQR_ERR_ARG for other leading dimensions, a misaligned pointer or another current device.
+ */
+typedef struct spanqr_graph_st* spanqr_graph_t;
+int spanqr_orth_graph_create(int K, int r, long long ldx, long long ldq, const float* Z, void* ws, size_t ws_bytes,
+                             spanqr_graph_t* graph);
+int spanqr_orth_graph_launch(spanqr_graph_t graph, const float* X, long long ldx, float* Q, long long ldq,
+                             spanqr_stream_t stream);
+int spanqr_orth_graph_destroy(spanqr_graph_t graph);
 
 /*
  * orth of one matrix for callers that cannot allocate device memory: code running inside a CUDA stream capture

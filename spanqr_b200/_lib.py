@@ -24,6 +24,9 @@ SIGNATURES = {
     "spanqr_read_status": (_I, [_P, _P, ctypes.POINTER(_I)]),
     "spanqr_orth_noalloc_f32": (_I, [_P, _LL, _P, _LL, _I, _I, _P, _P]),
     "spanqr_noalloc_read_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "spanqr_orth_graph_create": (_I, [_I, _I, _LL, _LL, _P, _P, _SZ, ctypes.POINTER(_P)]),
+    "spanqr_orth_graph_launch": (_I, [_P, _P, _LL, _P, _LL, _P]),
+    "spanqr_orth_graph_destroy": (_I, [_P]),
     "spanqr_gram_mode_f32": (_I, [_P, _LL, _I, _I, _P, _I, _P, _P, _SZ, _P]),
     "spanqr_timing_enable": (_I, [_I]),
     "spanqr_selftest_timeout": (_I, [_P, _SZ, _LL, _I, _P]),

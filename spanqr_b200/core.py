@@ -22,8 +22,8 @@ _Z = {}
 _WS = {}
 _GRAPHS = {}
 _lock = threading.RLock()
-# orth() replays one CUDA graph per (device, stream, shape): the ~30 launches of a call go to the GPU as one unit
-# (SPANQR_GRAPHS=0 launches them one by one instead)
+# orth() replays one CUDA graph per (device, stream, shape), created in the library, with the call's X and Q patched
+# in: the ~30 launches of a call go to the GPU as one unit (SPANQR_GRAPHS=0 launches them one by one instead)
 USE_GRAPHS = os.environ.get("SPANQR_GRAPHS", "1") != "0"
 
 
@@ -104,12 +104,12 @@ def orth(X: torch.Tensor) -> torch.Tensor:
     dev = X.device
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev)
+        Q = torch.empty((K, r), dtype=torch.float32, device=dev)
         if USE_GRAPHS:
             g = _graph(dev, stream, K, r)
-            g.x.copy_(X)
-            g.graph.replay()
-            return g.q.clone()
-        Q = torch.empty((K, r), dtype=torch.float32, device=dev)
+            _lib.check(_lib.lib().spanqr_orth_graph_launch(g.handle, X.data_ptr(), r, Q.data_ptr(), r,
+                                                           stream.cuda_stream), f"orth({K}x{r})")
+            return Q
         _call(X, Q, zdust(K, r, dev), workspace(dev, K, r, 1, stream), stream.cuda_stream)
     return Q
 
@@ -121,20 +121,25 @@ def _call(X, Q, Z, ws, stream_handle):
 
 
 class _Graph:
-    """one captured orth(K x r) with its own input, output and workspace (graphs bake in their pointers)"""
+    """one captured orth(K x r) call (spanqr_orth_graph_create) with its own workspace; each replay gets the call's X and
+    Q patched into its set-up kernel, so nothing is copied in or out"""
 
     def __init__(self, dev, stream, K, r, Z):
-        self.x = torch.zeros((K, r), dtype=torch.float32, device=dev)
-        self.q = torch.empty_like(self.x)
         self.ws = torch.empty(_lib.workspace_bytes(K, r, 1), dtype=torch.uint8, device=dev)
         self.z = Z
-        _call(self.x, self.q, self.z, self.ws, stream.cuda_stream)   # first run eagerly: kernels loaded, attributes set
-        self.graph = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream(dev)
-        cap.wait_stream(stream)
-        with torch.cuda.graph(self.graph, stream=cap):
-            _call(self.x, self.q, self.z, self.ws, cap.cuda_stream)
-        stream.wait_stream(cap)
+        x = torch.zeros((K, r), dtype=torch.float32, device=dev)
+        q = torch.empty_like(x)
+        _call(x, q, self.z, self.ws, stream.cuda_stream)   # first run eagerly: kernels loaded, attributes set
+        h = _lib.ctypes.c_void_p()
+        _lib.check(_lib.lib().spanqr_orth_graph_create(K, r, r, r, Z.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                                                       _lib.ctypes.byref(h)), f"orth graph ({K}x{r})")
+        self.handle = h
+
+    def __del__(self):
+        try:
+            _lib.lib().spanqr_orth_graph_destroy(self.handle)
+        except Exception:
+            pass
 
 
 def _graph(dev, stream, K, r):

@@ -286,6 +286,120 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
 
 }  // extern "C"
 
+// ---- orth as one CUDA graph per shape, X and Q patched per launch ----
+// Every kernel of an orth call reads the matrix pointers from the workspace table except the set-up kernel, which
+// writes them there: so a graph captured once per (K, r, ldx, ldq, Z, workspace) serves any X and Q after its set-up
+// node's arguments are replaced (cudaGraphExecKernelNodeSetParams affects only launches made after it).
+struct spanqr_graph_st {
+    int dev, K, r;
+    long long ldx, ldq;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    cudaGraphNode_t setup;
+    cudaKernelNodeParams base;   // the set-up node as captured (function, launch shape)
+    MatPtr* tab;
+    uint32_t* maxbits;
+    int* status;
+};
+
+extern "C" {
+
+int spanqr_orth_graph_create(int K, int r, long long ldx, long long ldq, const float* Z, void* ws, size_t ws_bytes,
+                             spanqr_graph_t* out) {
+    if (!out) return SPANQR_ERR_ARG;
+    *out = nullptr;
+    int rc = check_shape(K, r, 1);
+    if (rc) return rc;
+    if (!Z || !a16(Z) || ldx < r || ldq < r || ldx % 4 || ldq % 4) return SPANQR_ERR_ARG;
+    if ((rc = check_ws(ws, ws_bytes, K, r, 1))) return rc;
+    const Layout l = layout(K, r, 1);
+    spanqr_graph_st g{};
+    g.K = K;
+    g.r = r;
+    g.ldx = ldx;
+    g.ldq = ldq;
+    g.tab = at<MatPtr>(ws, l.ptrs);
+    g.maxbits = at<uint32_t>(ws, l.maxbits);
+    g.status = at<int>(ws, l.status);
+    cudaError_t e = cudaGetDevice(&g.dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    cudaStream_t cs = nullptr;
+    if ((e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking)) != cudaSuccess) return cuda_fail(e);
+    const int timing = g_timing;
+    g_timing = 0;   // no timing events inside the graph
+    e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        // the workspace stands in for X and Q until the first launch replaces them
+        cudaError_t le = launch_setup_strided(g.tab, static_cast<const float*>(ws), 0, static_cast<float*>(ws), 0, 1,
+                                              g.maxbits, g.status, cs);
+        rc = (le == cudaSuccess) ? run_orth(K, r, 1, ldx, ldq, Z, ws, cs) : cuda_fail(le);
+        e = cudaStreamEndCapture(cs, &g.graph);
+        if (rc == SPANQR_OK && e != cudaSuccess) rc = cuda_fail(e);
+    } else {
+        rc = cuda_fail(e);
+    }
+    g_timing = timing;
+    cudaStreamDestroy(cs);
+    if (rc == SPANQR_OK) {
+        size_t nn = 0;
+        e = cudaGraphGetNodes(g.graph, nullptr, &nn);
+        std::vector<cudaGraphNode_t> nodes(nn);
+        if (e == cudaSuccess && nn) e = cudaGraphGetNodes(g.graph, nodes.data(), &nn);
+        for (size_t i = 0; e == cudaSuccess && i < nn && !g.setup; ++i) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nodes[i], &t) != cudaSuccess || t != cudaGraphNodeTypeKernel) continue;
+            cudaKernelNodeParams kp{};
+            if (cudaGraphKernelNodeGetParams(nodes[i], &kp) == cudaSuccess && kp.func == setup_strided_kernel()) {
+                g.setup = nodes[i];
+                g.base = kp;
+            }
+        }
+        if (e == cudaSuccess && !g.setup) e = cudaErrorNotSupported;
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&g.exec, g.graph, 0);
+        if (e != cudaSuccess) rc = cuda_fail(e);
+    }
+    if (rc != SPANQR_OK) {
+        if (g.graph) cudaGraphDestroy(g.graph);
+        return rc;
+    }
+    *out = new spanqr_graph_st(g);
+    return SPANQR_OK;
+}
+
+int spanqr_orth_graph_launch(spanqr_graph_t g, const float* X, long long ldx, float* Q, long long ldq,
+                             spanqr_stream_t stream) {
+    if (!g || !X || !Q || !a16(X) || !a16(Q) || ldx != g->ldx || ldq != g->ldq) return SPANQR_ERR_ARG;
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev != g->dev) return SPANQR_ERR_ARG;
+    MatPtr* tab = g->tab;
+    const float* x = X;
+    float* q = Q;
+    long long stride = 0;
+    int B = 1;
+    uint32_t* maxbits = g->maxbits;
+    int* status = g->status;
+    void* args[8] = {&tab, &x, &stride, &q, &stride, &B, &maxbits, &status};   // k_setup_strided's parameters
+    cudaKernelNodeParams p = g->base;
+    p.kernelParams = args;
+    p.extra = nullptr;
+    e = cudaGraphExecKernelNodeSetParams(g->exec, g->setup, &p);
+    if (e == cudaSuccess) e = cudaGraphLaunch(g->exec, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_orth_graph_destroy(spanqr_graph_t g) {
+    if (!g) return SPANQR_OK;
+    cudaError_t e = cudaGraphExecDestroy(g->exec);
+    const cudaError_t e2 = cudaGraphDestroy(g->graph);
+    delete g;
+    if (e == cudaSuccess) e = e2;
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+}  // extern "C"
+
 // ---- orth without any allocation: scratch in a fixed array of the device image ----
 // For callers that may not call cudaMalloc (inside a stream capture that must not add allocations, in a
 // memory-capped sandbox, in a real-time loop).  The array belongs to the library's module: each GPU that loads the

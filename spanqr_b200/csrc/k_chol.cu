@@ -30,7 +30,7 @@ namespace {
 constexpr int LDT = TB + 1;         // a stored tile row, padded: the column walks of the products are conflict-free
 constexpr int TILE_F = TB * LDT;    // floats per stored tile
 constexpr int NT = 384;             // 12 warps (no register spills in the unrolled diagonal factor)
-constexpr int LA_THREADS = 64;      // look-ahead update of the next diagonal tile: 64 4 x 4 blocks, one per thread
+constexpr int LA_THREADS = 128;     // look-ahead group (warps 0-3): panel, update and factor of the next diagonal tile
 typedef float Tile[TB][LDT];
 
 // CTA q of C owns block rows q, q + C, q + 2C, ... < nb; row i's tiles (i, 0..i) sit in consecutive slots
@@ -49,9 +49,10 @@ __host__ __device__ __forceinline__ int max_tiles(int nb, int C) {
     for (int q = 0; q < C; ++q) m = tiles_of(nb, C, q) > m ? tiles_of(nb, C, q) : m;
     return m;
 }
-// own tiles, the panel slots (one per block row), the factored inverse, its local copy, the pivots' rsqrt, scalars
+// own tiles, the panel slots (one per block row), this step's Linv_j, the inverses of the own diagonal tiles, the
+// pivots' rsqrt, scalars
 __host__ __device__ __forceinline__ size_t smem_floats(int nb, int C) {
-    return (size_t)(max_tiles(nb, C) + nb + 2) * TILE_F + TB + 4;
+    return (size_t)(max_tiles(nb, C) + nb + 1 + rows_of(nb, C, 0)) * TILE_F + TB + 4;
 }
 
 __device__ __forceinline__ int cta_rank() {
@@ -73,25 +74,28 @@ __device__ __forceinline__ void sync_cluster() {
 }
 
 // factor the tile T in place with one warp (lane = row), T <- L tile (zeros above the diagonal); inv <- its inverse;
-// rd <- the pivots' reciprocal square roots (the operations of chol.cu:115-180)
+// rd <- the pivots' reciprocal square roots (the operations of chol.cu:115-180).  Lane i's entries right of its
+// diagonal are never read (lane i's l is 0 in the columns c > i, and they are zeroed at the end), so the update
+// a_ik -= l_i l_k runs on every lane without the reference's select; and the next pivot, lane c + 1's updated
+// diagonal, is computed from lane c + 1's own l (the same fused multiply-add) before the other lanes' l_{c+1} arrive,
+// which keeps one shuffle off the column-to-column chain.
 __device__ void factor_warp(float (*T)[LDT], float (*inv)[LDT], float* rd, float tau) {
     const int i = threadIdx.x & 31;
     float a[TB];
 #pragma unroll
     for (int k = 0; k < TB; ++k) a[k] = T[i][k];
     float myrd = 0.0f;
+    float pnext = a[0];   // lane c's diagonal entry, current before column c
 #pragma unroll
     for (int c = 0; c < TB; ++c) {
-        const float piv = fmaxf(__shfl_sync(0xffffffffu, a[c], c), tau);
+        const float piv = fmaxf(__shfl_sync(0xffffffffu, pnext, c), tau);
         const float r = det_rsqrt(piv);
         const float l = (i > c) ? __fmul_rn(a[c], r) : ((i == c) ? __fmul_rn(piv, r) : 0.0f);
         myrd = (i == c) ? r : myrd;
         a[c] = l;
+        if (c + 1 < TB) pnext = __fmaf_rn(-l, l, a[c + 1]);   // on lane c + 1: a_{c+1,c+1} - l_{c+1}^2
 #pragma unroll
-        for (int k = c + 1; k < TB; ++k) {
-            const float lk = __shfl_sync(0xffffffffu, l, k);
-            a[k] = __fmaf_rn(-((i >= k) ? l : 0.0f), lk, a[k]);
-        }
+        for (int k = c + 1; k < TB; ++k) a[k] = __fmaf_rn(-l, __shfl_sync(0xffffffffu, l, k), a[k]);
     }
 #pragma unroll
     for (int k = 0; k < TB; ++k) T[i][k] = (k <= i) ? a[k] : 0.0f;
@@ -118,43 +122,64 @@ __device__ void factor_warp(float (*T)[LDT], float (*inv)[LDT], float* rd, float
     __syncwarp();
 }
 
-// acc[u][v] = sum_m X[r0+u][m] Y[c0+v][m] for a 4 x 4 block, FMA chains from zero, m in order (chol.cu:63-71)
-__device__ __forceinline__ void mm44_at(const float (*X)[LDT], const float (*Y)[LDT], int r0, int c0, float acc[4][4]) {
+// acc[u][v] = sum_m X[r0+u][m] Y[c0+v][m] for an RU x RV block, FMA chains from zero, m in order (chol.cu:63-71)
+template <int RU, int RV>
+__device__ __forceinline__ void mm_at(const float (*X)[LDT], const float (*Y)[LDT], int r0, int c0,
+                                      float (&acc)[RU][RV]) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < RU; ++u)
 #pragma unroll
-        for (int v = 0; v < 4; ++v) acc[u][v] = 0.0f;
+        for (int v = 0; v < RV; ++v) acc[u][v] = 0.0f;
 #pragma unroll 4
     for (int m = 0; m < TB; ++m) {
-        float x[4], y[4];
+        float x[RU], y[RV];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = X[r0 + u][m];
+        for (int u = 0; u < RU; ++u) x[u] = X[r0 + u][m];
 #pragma unroll
-        for (int v = 0; v < 4; ++v) y[v] = Y[c0 + v][m];
+        for (int v = 0; v < RV; ++v) y[v] = Y[c0 + v][m];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < RU; ++u)
 #pragma unroll
-            for (int v = 0; v < 4; ++v) acc[u][v] = __fmaf_rn(x[u], y[v], acc[u][v]);
+            for (int v = 0; v < RV; ++v) acc[u][v] = __fmaf_rn(x[u], y[v], acc[u][v]);
     }
 }
 
-// T -= acc on a 4 x 4 block
-__device__ __forceinline__ void sub44(float (*T)[LDT], int r0, int c0, const float acc[4][4]) {
+// T -= acc on an RU x RV block
+template <int RU, int RV>
+__device__ __forceinline__ void sub_at(float (*T)[LDT], int r0, int c0, const float (&acc)[RU][RV]) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < RU; ++u)
 #pragma unroll
-        for (int v = 0; v < 4; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
+        for (int v = 0; v < RV; ++v) T[r0 + u][c0 + v] = __fsub_rn(T[r0 + u][c0 + v], acc[u][v]);
 }
 
-// one warp stores the factored diagonal tile j and its inverse (coalesced rows)
-__device__ __forceinline__ void store_diag(float* L, float* Li, int n, int j, const float (*T)[LDT],
-                                           const float (*inv)[LDT]) {
-    for (int e = threadIdx.x & 31; e < TB * TB; e += 32) {
-        const int r = e / TB, c = e % TB;
-        L[(size_t)(j * TB + r) * n + j * TB + c] = T[r][c];
-        Li[(size_t)(j * TB + r) * TB + c] = inv[r][c];
-    }
+// a panel block into its panel slot
+template <int RU>
+__device__ __forceinline__ void put_panel(float (*slot)[LDT], int r0, int c0, const float (&acc)[RU][4]) {
+#pragma unroll
+    for (int u = 0; u < RU; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) slot[r0 + u][c0 + v] = acc[u][v];
 }
+
+// split phases of the cluster barrier (C = 1: of named barrier 2 over the CTA): arrive releases this thread's
+// writes, wait acquires every arriving thread's
+template <int C>
+__device__ __forceinline__ void step_arrive() {
+    if constexpr (C > 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    else asm volatile("bar.arrive 2, %0;" ::"n"(NT) : "memory");
+}
+template <int C>
+__device__ __forceinline__ void step_arrive_wait() {
+    if constexpr (C > 1)
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    else asm volatile("bar.sync 2, %0;" ::"n"(NT) : "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 }  // namespace
 
 template <int C>
@@ -169,9 +194,9 @@ __global__ void __launch_bounds__(NT, 1) k_chol_dsm(float* __restrict__ A_all, f
     const int tid = threadIdx.x, warp = tid >> 5;
     Tile* T = reinterpret_cast<Tile*>(smem4);   // own tiles
     Tile* PB = T + max_tiles(nb, C);            // PB[i]: the panel P_i of the current step
-    Tile& INV = PB[nb];                         // the inverse this CTA factored last (read by the others)
-    Tile& LINV = PB[nb + 1];                    // this step's Linv_j
-    float* rd = &PB[nb + 2][0][0];
+    Tile& LINV = PB[nb];                        // this step's Linv_j
+    Tile* IV = PB + nb + 1;                     // IV[t]: the inverse of own diagonal tile q + C t (read by the others)
+    float* rd = &IV[rows_of(nb, C, 0)][0][0];
     float* misc = rd + TB;                      // [0] tau, [1] shift
     const float* A = A_all + (size_t)b * n * n;
     float* L = L_all + (size_t)b * n * n;
@@ -182,7 +207,7 @@ __global__ void __launch_bounds__(NT, 1) k_chol_dsm(float* __restrict__ A_all, f
     // in-order fp64 sum below does not wait on one global load per term
     double* rs = reinterpret_cast<double*>(&PB[0][0][0]);
     if (rowsq && tid < nsq) rs[tid] = rowsq[(size_t)b * n + tid];
-    // own block rows of A (float4 reads, 4 in flight per thread); upper tiles of L zeroed on request
+    // own block rows of A (float4 reads, 4 in flight per thread)
     for (int t = 0; t < nr; ++t) {
         const int i = q + C * t, w4 = 8 * (i + 1), tot = TB * w4;   // float4s of row i's tiles
         Tile* Ti = T + row_slot(C, q, i);
@@ -203,12 +228,6 @@ __global__ void __launch_bounds__(NT, 1) k_chol_dsm(float* __restrict__ A_all, f
                     d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
                 }
             }
-        }
-        if (zero_upper) {
-            const int z4 = (n - TB * (i + 1)) / 4;   // float4s right of the diagonal tile in each row of the block
-            for (int e = tid; e < TB * z4; e += NT)
-                *reinterpret_cast<float4*>(L + (size_t)(i * TB + e / z4) * n + TB * (i + 1) + 4 * (e % z4)) =
-                    make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
     __syncthreads();
@@ -239,64 +258,60 @@ __global__ void __launch_bounds__(NT, 1) k_chol_dsm(float* __restrict__ A_all, f
         }
         __syncthreads();
     }
-    if (q == 0 && warp == 0) {
-        factor_warp(T[0], INV, rd, tau);
-        store_diag(L, Li, n, 0, T[0], INV);
-    }
+    if (q == 0 && warp == 0) factor_warp(T[0], IV[0], rd, tau);
 
     for (int j = 0; j < nb; ++j) {
-        sync_cluster<C>();   // Linv_j is complete in its owner's INV; every update of step j - 1 is done
+        sync_cluster<C>();   // Linv_j is complete in its owner's IV slot; every update of step j - 1 is done
         if (j + 1 == nb) break;
-        {   // Linv_j from its owner
-            const float4* src = reinterpret_cast<const float4*>(&INV[0][0]);
+        {   // Linv_j from its owner (slot j / C there)
+            const float4* src = reinterpret_cast<const float4*>(&IV[j / C][0][0]);
             if (C > 1) src = on_rank(src, j % C);
             float4* dst = reinterpret_cast<float4*>(&LINV[0][0]);
             for (int e = tid; e < TILE_F / 4; e += NT) dst[e] = src[e];
         }
         __syncthreads();
-        // panels of this CTA's rows i > j: P_i = A[i, j] Linv_j^T into PB[i], and to L[i, j]
-        const int t0 = (j + 1 - q + C - 1) / C;   // first own row index t with q + C t > j
-        const int npan = (nr - t0) * 64;
-        for (int w = tid; w < npan; w += NT) {
-            const int i = q + C * (t0 + w / 64), r0 = 4 * ((w % 64) / 8), c0 = 4 * (w % 8);
-            float acc[4][4];
-            mm44_at(T[row_slot(C, q, i) + j], LINV, r0, c0, acc);
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-#pragma unroll
-                for (int v = 0; v < 4; ++v) PB[i][r0 + u][c0 + v] = acc[u][v];
-                *reinterpret_cast<float4*>(L + (size_t)(i * TB + r0 + u) * n + j * TB + c0) =
-                    make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
-            }
-        }
-        sync_cluster<C>();   // every panel of step j is complete
-        if (C > 1) {   // the other CTAs' panels P_k, k > j
-            const int cnt = nb - 1 - j;
-            for (int e = tid; e < cnt * (TILE_F / 4); e += NT) {
-                const int k = j + 1 + e / (TILE_F / 4), f = e % (TILE_F / 4);
-                if (k % C == q) continue;
-                const float4* src = on_rank(reinterpret_cast<const float4*>(&PB[k][0][0]) + f, k % C);
-                reinterpret_cast<float4*>(&PB[k][0][0])[f] = *src;
-            }
-            __syncthreads();
-        }
         const int j1 = j + 1;
-        const bool la = (j1 % C) == q;   // this CTA owns row j + 1: look-ahead on the first two warps
-        if (la && tid < LA_THREADS) {
-            float (*Tj)[LDT] = T[row_slot(C, q, j1) + j1];
-            const int r0 = 4 * (tid / 8), c0 = 4 * (tid % 8);
-            float acc[4][4];
-            mm44_at(PB[j1], PB[j1], r0, c0, acc);
-            sub44(Tj, r0, c0, acc);
-            asm volatile("bar.sync 1, %0;" ::"n"(LA_THREADS) : "memory");
-            if (warp == 0) {
-                factor_warp(Tj, INV, rd, tau);
-                store_diag(L, Li, n, j1, Tj, INV);
-            }
+        const bool la = (j1 % C) == q;            // this CTA owns row j + 1
+        const int t0 = (j + 1 - q + C - 1) / C;   // first own row index t with q + C t > j (on the la CTA, row j + 1)
+        if (la && warp < LA_THREADS / 32) {
+            // look-ahead group: P_{j+1} = A[j+1, j] Linv_j^T, released to the cluster at once; then tile (j+1, j+1)
+            // -= P_{j+1} P_{j+1}^T and its factorisation, while the other warps of the cluster do the rest of the step
+            const int r0 = 2 * (tid / 8), c0 = 4 * (tid % 8);
+            const int s1 = row_slot(C, q, j1);
+            float acc[2][4];
+            mm_at<2, 4>(T[s1 + j], LINV, r0, c0, acc);
+            put_panel<2>(PB[j1], r0, c0, acc);
+            step_arrive<C>();
+            named_sync(1, LA_THREADS);
+            mm_at<2, 4>(PB[j1], PB[j1], r0, c0, acc);
+            sub_at<2, 4>(T[s1 + j1], r0, c0, acc);
+            named_sync(1, LA_THREADS);
+            if (warp == 0) factor_warp(T[s1 + j1], IV[j1 / C], rd, tau);
+            if (C > 1) cluster_wait();
         } else {
-            // A[i, k] -= P_i P_k^T for own rows i > j and j < k <= i, except (j + 1, j + 1) on the look-ahead CTA
-            const int wid = la ? tid - LA_THREADS : tid, nw = la ? NT - LA_THREADS : NT;
-            // own rows from t0 on hold i - j trailing tiles each (k = j + 1 .. i); task = 64 blocks per tile
+            const int nw = la ? NT - LA_THREADS : NT, wid = la ? tid - LA_THREADS : tid;
+            // panels of this CTA's other rows i > j: P_i = A[i, j] Linv_j^T into PB[i], and to L[i, j]
+            const int tp = la ? t0 + 1 : t0;
+            for (int w = wid; w < (nr - tp) * 64; w += nw) {
+                const int i = q + C * (tp + w / 64), r0 = 4 * ((w % 64) / 8), c0 = 4 * (w % 8);
+                float acc[4][4];
+                mm_at<4, 4>(T[row_slot(C, q, i) + j], LINV, r0, c0, acc);
+                put_panel<4>(PB[i], r0, c0, acc);
+            }
+            step_arrive_wait<C>();   // every panel of step j is complete
+            // the other CTAs' panels P_k (k > j) into this CTA's slots; this CTA's panels in place of A[i, j] (they
+            // are L[i, j]; nothing reads column j again, and every global store of L waits until the end of the
+            // kernel, so that no barrier's release has to wait for global writes)
+            const int cnt = nb - 1 - j;
+            for (int e = wid; e < cnt * (TILE_F / 4); e += nw) {
+                const int k = j + 1 + e / (TILE_F / 4), f = e % (TILE_F / 4);
+                float4* slot = reinterpret_cast<float4*>(&PB[k][0][0]) + f;
+                if (k % C == q) reinterpret_cast<float4*>(&T[row_slot(C, q, k) + j][0][0])[f] = *slot;
+                else if (C > 1) *slot = *on_rank(slot, k % C);
+            }
+            named_sync(3, nw);
+            // A[i, k] -= P_i P_k^T for own rows i > j and j < k <= i, except (j + 1, j + 1) on the look-ahead CTA;
+            // own rows from t0 on hold i - j trailing tiles each (k = j + 1 .. i), 64 4 x 4 blocks per tile
             int ntask = 0;
             for (int t = t0; t < nr; ++t) ntask += (q + C * t - j) * 64;
             for (int w = wid; w < ntask; w += nw) {
@@ -306,12 +321,31 @@ __global__ void __launch_bounds__(NT, 1) k_chol_dsm(float* __restrict__ A_all, f
                     ++t;
                 }
                 const int i = q + C * t, k = j + 1 + x;
-                if (la && i == j1) continue;   // that is the look-ahead tile (k = j1 is the only tile of row j1)
+                if (la && i == j1) continue;   // the look-ahead tile (k = j1 is the only trailing tile of row j1)
                 const int r0 = 4 * ((w % 64) / 8), c0 = 4 * (w % 8);
                 float acc[4][4];
-                mm44_at(PB[i], PB[k], r0, c0, acc);
-                sub44(T[row_slot(C, q, i) + k], r0, c0, acc);
+                mm_at<4, 4>(PB[i], PB[k], r0, c0, acc);
+                sub_at<4, 4>(T[row_slot(C, q, i) + k], r0, c0, acc);
             }
+        }
+    }
+    // every tile of this CTA's block rows is final: L[i, 0..i], the inverse of tile (i, i), zeros right of it on request
+    for (int t = 0; t < nr; ++t) {
+        const int i = q + C * t, w4 = 8 * (i + 1), z4 = zero_upper ? (n - TB * (i + 1)) / 4 : 0;
+        const Tile* Ti = T + row_slot(C, q, i);
+        for (int e = tid; e < TB * (w4 + z4); e += NT) {
+            const int r = e / (w4 + z4), c = 4 * (e % (w4 + z4));
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (c < TB * (i + 1)) {
+                const float* s = &Ti[c / TB][r][c % TB];
+                v = make_float4(s[0], s[1], s[2], s[3]);
+            }
+            *reinterpret_cast<float4*>(L + (size_t)(i * TB + r) * n + c) = v;
+        }
+        for (int e = tid; e < TB * TB / 4; e += NT) {
+            const int r = e / (TB / 4), c = 4 * (e % (TB / 4));
+            const float* s = &IV[t][r][c];
+            *reinterpret_cast<float4*>(Li + (size_t)(i * TB + r) * TB + c) = make_float4(s[0], s[1], s[2], s[3]);
         }
     }
 }

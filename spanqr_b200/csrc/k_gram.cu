@@ -29,12 +29,21 @@ __global__ void __launch_bounds__(256) k_gram_reduce(const float* __restrict__ P
     for (int q = threadIdx.x; q < RSTRIP * T / 4; q += blockDim.x) {
         const int r = q / (T / 4), c = 4 * (q % (T / 4));
         double t0 = 0.0, t1 = 0.0, t2 = 0.0, t3 = 0.0;
-        for (int sp = 0; sp < gp.S; ++sp) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + sp * split_stride + (size_t)r * T + c));
-            t0 = __dadd_rn(t0, (double)v.x);
-            t1 = __dadd_rn(t1, (double)v.y);
-            t2 = __dadd_rn(t2, (double)v.z);
-            t3 = __dadd_rn(t3, (double)v.w);
+        // eight splits' loads in flight at a time; the sums still run in split order
+        for (int sp0 = 0; sp0 < gp.S; sp0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (sp0 + u < gp.S)
+                    v[u] = __ldcg(reinterpret_cast<const float4*>(src + (size_t)(sp0 + u) * split_stride + (size_t)r * T + c));
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (sp0 + u < gp.S) {
+                    t0 = __dadd_rn(t0, (double)v[u].x);
+                    t1 = __dadd_rn(t1, (double)v[u].y);
+                    t2 = __dadd_rn(t2, (double)v[u].z);
+                    t3 = __dadd_rn(t3, (double)v[u].w);
+                }
         }
         const int a = ti * T + r0 + r;
         float g[4] = {__double2float_rn(t0), __double2float_rn(t1), __double2float_rn(t2), __double2float_rn(t3)};

@@ -68,6 +68,8 @@ __global__ void __launch_bounds__(256) k_absmax(PtrArg p, int K, int r, long lon
 
 int setup_host_launches(int B) { return (B + HOST_CHUNK - 1) / HOST_CHUNK; }
 
+const void* setup_strided_kernel() { return reinterpret_cast<const void*>(&k_setup_strided); }
+
 cudaError_t launch_setup_strided(MatPtr* tab, const float* X, long long sX, float* Q, long long sQ, int B,
                                  uint32_t* maxbits, int* status, cudaStream_t st) {
     k_setup_strided<<<cdiv(B, 128), 128, 0, st>>>(tab, X, sX, Q, sQ, B, maxbits, status);

@@ -31,6 +31,9 @@ struct GramPlan {
     int KS;      // rows per split
 };
 
+// the set-up kernel of the strided entry points, k_setup_strided(tab, X, sX, Q, sQ, B, maxbits, status): the only
+// kernel of an orth call that takes X and Q as arguments (every later one reads them from the table)
+const void* setup_strided_kernel();
 cudaError_t launch_setup_strided(MatPtr* tab, const float* X, long long sX, float* Q, long long sQ, int B,
                                  uint32_t* maxbits, int* status, cudaStream_t st);
 cudaError_t launch_setup_array(MatPtr* tab, const float* const* dX, float* const* dQ, int B, uint32_t* maxbits,

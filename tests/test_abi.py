@@ -62,6 +62,13 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_gram_mode_f32(al, 64, 256, 64, None, 3, al, al, 10 ** 9, None) == ARG      # no such mode
     assert L.spanqr_gram_mode_f32(al, 64, 32, 64, None, 1, al, al, 10 ** 9, None) == SHAPE     # K < n
     assert L.spanqr_gram_mode_f32(al, 64, 256, 64, None, 2, al, al, ws_need - 1, None) == WS   # workspace too small
+    h = ctypes.c_void_p()
+    assert L.spanqr_orth_graph_create(256, 100, 100, 100, al, al, 10 ** 9, ctypes.byref(h)) == SHAPE
+    assert L.spanqr_orth_graph_create(256, 64, 64, 64, al + 4, al, 10 ** 9, ctypes.byref(h)) == ARG   # misaligned Z
+    assert L.spanqr_orth_graph_create(256, 64, 64, 64, al, al, ws_need - 1, ctypes.byref(h)) == WS
+    assert L.spanqr_orth_graph_create(256, 64, 64, 64, al, al, ws_need, None) == ARG
+    assert L.spanqr_orth_graph_launch(None, al, 64, al, 64, None) == ARG
+    assert L.spanqr_orth_graph_destroy(None) == OK
     st = ctypes.c_int(7)
     assert L.spanqr_read_status(None, None, ctypes.byref(st)) == ARG
     assert L.spanqr_noalloc_read_status(None, None) == ARG

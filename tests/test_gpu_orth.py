@@ -137,6 +137,27 @@ def test_graph_replay_equals_eager_launches():
             assert gu.bits_equal(g.cpu().numpy(), want.cpu().numpy()), (K, r)
 
 
+def test_graph_patches_x_and_q_per_launch():
+    """one graph serves calls on different inputs and outputs (only the set-up kernel's X and Q change): interleaved
+    calls on two matrices give each its eager bits, and a call's output buffer is the one returned"""
+    from spanqr_b200 import core
+    K, r = 2048, 256
+    X1 = cases.make_case(K, r, "mixed_c2").cuda()
+    X2 = cases.make_case(K, r, "ttf_cu4_t1e-2").cuda()
+    saved = core.USE_GRAPHS
+    try:
+        core.USE_GRAPHS = False
+        want1, want2 = orth(X1), orth(X2)
+        core.USE_GRAPHS = True
+        got = [orth(X1), orth(X2), orth(X2), orth(X1)]
+    finally:
+        core.USE_GRAPHS = saved
+    torch.cuda.synchronize()
+    assert len({q.data_ptr() for q in got}) == 4
+    for g, w in zip(got, [want1, want2, want2, want1]):
+        assert gu.bits_equal(g.cpu().numpy(), w.cpu().numpy())
+
+
 def test_kernel_timer_modes_count_the_same_launches():
     """the event timer and the count-only timer see the same launches of the same kinds; count-only adds no time"""
     from spanqr_b200 import _lib, orth_batched

@@ -20,6 +20,7 @@
  *   spanqr_orth_batched_f32  no reference counterpart: same, from device arrays of matrix pointers
  *   spanqr_orth_ptrs_f32     no reference counterpart: same, from host arrays of matrix pointers
  *   spanqr_orth_graph_*      no reference counterpart: spanqr_orth_f32 captured once per shape, replayed per call
+ *   spanqr_orth_mixed_f32    no reference counterpart: a batch of layers of one width and different heights
  *   spanqr_gram_f32          candidates/tri.py:362-375 gram_f(Y, s) and tri.py:285-297 gram_split(Y, bt=64)
  *   spanqr_gram_mode_f32     the same, and kcholqr.py:106 Y.T @ Y (each Gram of the orth sequence on its own)
  *   spanqr_chol_f32          candidates/kchol.py:35-44 chol32(G, tau) (kernel candidates/cuk/chol.cu:273-276)
@@ -81,6 +82,17 @@ int spanqr_orth_batched_f32(const float* const* dX, float* const* dQ, int K, int
  * host-to-device copy and no pinned memory is involved; leading dimension r for all) */
 int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r, int batch, const float* Z,
                          void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * orth of `batch` matrices of one width r and per-matrix heights K[b] (host arrays hX, hQ of device pointers with
+ * leading dimension r, host array K, host array Z of per-matrix dust pointers: Z[b] is the dust of shape K[b] x r,
+ * the same pointer for equal heights).  The workspace (spanqr_workspace_bytes_mixed) holds one batched call per
+ * distinct height; the groups run one after another on `stream`, and each matrix gets the bits of a lone
+ * spanqr_orth_f32 call.  No reference counterpart (the reference orthonormalises one layer at a time).
+ */
+int spanqr_workspace_bytes_mixed(const int* K, int r, int batch, size_t* bytes);
+int spanqr_orth_mixed_f32(const float* const* hX, float* const* hQ, const int* K, int r, int batch,
+                          const float* const* Z, void* ws, size_t ws_bytes, spanqr_stream_t stream);
 
 /*
  * orth of one shape as one CUDA graph (no reference counterpart; the reference launches kernel by kernel from Python,

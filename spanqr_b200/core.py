@@ -79,17 +79,19 @@ def orth(X: torch.Tensor) -> torch.Tensor:
     rank-deficient or zero, the missing directions are completed with arbitrary orthonormal ones (never zero or NaN
     columns).  Deterministic, no host sync, X left untouched.  Above r 512 with r a multiple of 256 the columns go
     through block Gram-Schmidt over 256-column blocks (orth.py:18-19, spanqr_b200.big.borth).  r % 32 != 0 is
-    padded with zero columns to the next multiple of 32 (K must reach it) and the first r columns returned."""
+    padded with zero columns to the next multiple of 32, and r > 512 that is not a multiple of 256 to the next multiple
+    of 256 (K must reach it); the first r columns are returned."""
     if torch.is_tensor(X) and X.dim() == 2 and X.shape[1] > 0 and (X.shape[1] % TB or X.shape[1] > MAX_R):
         if X.dtype != torch.float32 or not X.is_cuda:
             raise TypeError(f"X must be an fp32 CUDA tensor (got {X.dtype} on {X.device})")
         K, r = X.shape
-        if r % TB:
+        if r % TB or (r > MAX_R and r % 256):
             # padded tiles instead of the reference's Householder fallback (kcholqr.py:98-99): zero columns up to
-            # the next multiple of 32 (of 256 above 512); the solve is triangular, so Q's first r columns span X
+            # the next multiple of 32 (of 256 above 512, where the reference runs kcholqr_f at full width,
+            # orth.py:18-20, and this build goes blockwise); the solves are triangular, so Q's first r columns span X
             rp = -(-r // TB) * TB if r <= MAX_R else -(-r // 256) * 256
             if K < rp:
-                raise ValueError(f"unsupported shape {K}x{r}: r % {TB} != 0 needs K >= {rp} (r padded to {rp})")
+                raise ValueError(f"unsupported shape {K}x{r}: r is padded to {rp} here, which needs K >= {rp}")
             Xp = torch.zeros((K, rp), dtype=torch.float32, device=X.device)
             Xp[:, :r] = X
             return orth(Xp)[:, :r].contiguous()

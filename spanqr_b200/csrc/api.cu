@@ -286,6 +286,82 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
 
 }  // extern "C"
 
+// ---- a batch of matrices of one width and different heights ----
+// Matrices are grouped by K in order of first appearance; group g runs as one batched orth over its own slice of the
+// workspace, the groups one after another on the stream.  Each matrix gets the bits of a lone spanqr_orth_f32 call.
+namespace {
+struct KGroups {
+    std::vector<int> K;                 // distinct heights, in order of first appearance
+    std::vector<std::vector<int>> idx;  // the matrices of each height, in index order
+};
+
+int group_by_K(const int* K, int r, int batch, KGroups& g) {
+    if (!K || batch < 1) return SPANQR_ERR_SHAPE;
+    for (int b = 0; b < batch; ++b) {
+        size_t i = 0;
+        while (i < g.K.size() && g.K[i] != K[b]) ++i;
+        if (i == g.K.size()) {
+            g.K.push_back(K[b]);
+            g.idx.emplace_back();
+        }
+        g.idx[i].push_back(b);
+    }
+    for (size_t i = 0; i < g.K.size(); ++i) {
+        const int rc = check_shape(g.K[i], r, (int)g.idx[i].size());
+        if (rc) return rc;
+    }
+    return SPANQR_OK;
+}
+
+size_t mixed_bytes(const KGroups& g, int r) {
+    size_t t = 0;
+    for (size_t i = 0; i < g.K.size(); ++i) t += al256(layout(g.K[i], r, (int)g.idx[i].size()).total);
+    return t;
+}
+}  // namespace
+
+extern "C" {
+
+int spanqr_workspace_bytes_mixed(const int* K, int r, int batch, size_t* bytes) {
+    if (!bytes) return SPANQR_ERR_ARG;
+    KGroups g;
+    const int rc = group_by_K(K, r, batch, g);
+    if (rc) return rc;
+    *bytes = mixed_bytes(g, r);
+    return SPANQR_OK;
+}
+
+int spanqr_orth_mixed_f32(const float* const* hX, float* const* hQ, const int* K, int r, int batch,
+                          const float* const* Z, void* ws, size_t ws_bytes, spanqr_stream_t stream) {
+    KGroups g;
+    int rc = group_by_K(K, r, batch, g);
+    if (rc) return rc;
+    if (!hX || !hQ || !Z) return SPANQR_ERR_ARG;
+    for (size_t i = 0; i < g.K.size(); ++i)
+        for (int b : g.idx[i])   // one dust per height
+            if (!Z[b] || Z[b] != Z[g.idx[i][0]]) return SPANQR_ERR_ARG;
+    if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0 || ws_bytes < mixed_bytes(g, r)) return SPANQR_ERR_WORKSPACE;
+    char* w = static_cast<char*>(ws);
+    std::vector<const float*> xs;
+    std::vector<float*> qs;
+    for (size_t i = 0; i < g.K.size(); ++i) {
+        const int Bg = (int)g.idx[i].size();
+        xs.clear();
+        qs.clear();
+        for (int b : g.idx[i]) {
+            xs.push_back(hX[b]);
+            qs.push_back(hQ[b]);
+        }
+        const size_t need = al256(layout(g.K[i], r, Bg).total);
+        rc = spanqr_orth_ptrs_f32(xs.data(), qs.data(), g.K[i], r, Bg, Z[g.idx[i][0]], w, need, stream);
+        if (rc) return rc;
+        w += need;
+    }
+    return SPANQR_OK;
+}
+
+}  // extern "C"
+
 // ---- orth as one CUDA graph per shape, X and Q patched per launch ----
 // Every kernel of an orth call reads the matrix pointers from the workspace table except the set-up kernel, which
 // writes them there: so a graph captured once per (K, r, ldx, ldq, Z, workspace) serves any X and Q after its set-up

@@ -3,10 +3,7 @@
 // The reference's 32-column block recurrence Y_j = (A_j - sum_{k<j} Y_k L_jk^T) Li_j^T is evaluated as
 //     Y_j = A_j W_jj^T + sum_{k<j} Y_k W_jk^T,   W_jj = Li_j,  W_jk = -Li_j L_jk   (k_trsm_w.cu builds W),
 // right-looking: every block's accumulator lives in TMEM from the start (n <= 256: 8 blocks x 32 columns, a large
-// hi.hi accumulator and a small hi.lo + lo.hi one, 512 columns), zeroed once, and every product adds to it.  As soon
-// as Y_j is known, one product Y_j [W_{j+1, j}; ...; W_{nb-1, j}]^T (N up to 224) updates all later blocks, so the
-// chain from one block to the next is only: read the accumulator, split the block into shared memory, block j+1's
-// own product and that update (a tcgen05.mma costs about the same for N = 32 as for N = 224).
+// hi.hi accumulator and a small hi.lo + lo.hi one, 512 columns), zeroed once, and every product adds to it.
 // One CTA = 128 rows of one matrix, in four warp roles:
 //   warps 0-3  epilogue: TMEM lanes 0-127 = the CTA's rows; block j's accumulators -> Y_j -> output rows and the
 //              tf32 hi/lo operand of the update;
@@ -15,6 +12,12 @@
 //   warp 8     one thread issues every product, in a fixed order, so the result does not depend on timing;
 //   warp 9     one thread issues every copy: row tiles through the per-matrix tensor maps, W tiles by bulk copy (a
 //              copy can hold its issuing thread for a microsecond, which must not delay the products).
+// Block c's row tile, its operand and later Y_c share one slot of a ring of three (raw -> hi | lo -> Y_c hi | lo), so
+// the update by Y_j never waits for a buffer the next block needs.  Product order, fixed in code:
+//   diag(0); [ACC]; then for j = 0 .. nb-2:  diag(j+1) (before Y_j exists: it overlaps block j's epilogue);
+//   T1(j) = Y_j W_{j+1,j}^T into block j+1 (32 columns); [ACC: block j+1 complete];
+//   T2(j) = Y_j W_{j+2.., j}^T into the later blocks (one product, N up to 192); [FREE of slot j % 3];
+// so the chain from one block to the next is the epilogue and T1 alone.
 // The output block j is written to Q (in place in passes 2 and 3: block j was read before, later blocks are untouched).
 // One launch solves one panel of at most 8 blocks, j0 .. j0 + nbp - 1, of a matrix of NB = n / 32 blocks (W indexed in
 // the whole image); a second panel starts its accumulators from `init`, the first panel's contribution
@@ -33,24 +36,30 @@ constexpr int BLK = 32;
 constexpr int MAXNB = 8;
 constexpr int YT = ROWS * 128;                  // 128 rows x 32 fp32 (raw) or tf32 (operand): 16 KB
 constexpr int WPART = 4096;                     // 32 x 32 tf32 operand tile
-constexpr int OFF_AB = 0;                       // two A buffers [raw x | raw z] -> [hi | lo]: 64 KB
-constexpr int OFF_YJ = OFF_AB + 2 * 2 * YT;     // Y_j [hi | lo]: 32 KB
-constexpr int OFF_WD = OFF_YJ + 2 * YT;         // two diagonal W tiles [hi | lo]: 16 KB
+constexpr int NSLOT = 3;                        // row-block slots [raw x | raw z] -> [hi | lo] -> [Y hi | Y lo]
+constexpr int SLOT = 2 * YT;
+constexpr int OFF_AB = 0;
+constexpr int OFF_WD = OFF_AB + NSLOT * SLOT;   // two diagonal W tiles [hi | lo]: 16 KB
 constexpr int OFF_WT = OFF_WD + 2 * 2 * WPART;  // two trailing W columns [hi tiles | lo tiles]: 2 x 56 KB
 constexpr int WTBUF = (MAXNB - 1) * 2 * WPART;
 constexpr int OFF_BAR = OFF_WT + 2 * WTBUF;
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int BAR_BYTES = 512;
+constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;
 constexpr uint32_t TCOLS = 512;                 // block c: large at 32 c, small at 256 + 32 c
 constexpr int ERR_TIMEOUT = 0x40;
-// mbarriers: raw A landed (x2), diagonal W landed (x2), trailing W landed (x2), A converted (x2, 128 arrivals),
-// Y_j stored (128 arrivals), accumulator of the next block complete (and Y_j's update done), the same event for the
-// copy warp, error drain.  A parity wait is only meaningful for the phase in progress or the one just completed:
-// every waiter below steps through its barrier's phases in order from phase 0, and no barrier can run two phases
-// ahead of a waiter, because its next phase needs something that waiter has not yet released.
-enum { B_A = 0, B_WD = 2, B_WT = 4, B_CONV = 6, B_Y = 8, B_ACC = 9, B_FREE = 10, B_FIN = 11, NBAR = 12 };
-__device__ __forceinline__ uint32_t ring_parity(int c) { return (uint32_t)((c >> 1) & 1); }   // c-th use of a 2-ring
+// mbarriers: row tile landed (per slot), diagonal W landed (x2), trailing W landed (x2), operand converted (per slot,
+// 128 arrivals), Y_j stored (128 arrivals), accumulator of the next block complete, slot released (per slot: T1 and
+// T2 of its Y and everything issued before them done), error drain.  A parity wait is only meaningful for the phase
+// in progress or the one just completed: every waiter below steps through its barrier's phases in order from phase 0,
+// and no barrier can run two phases ahead of a waiter, because its next phase needs something that waiter has not yet
+// released (the copy thread's one wait on ACC phase 0 comes before it issues the diagonal tile that ACC phase 2
+// needs).
+enum { B_A = 0, B_WD = 3, B_WT = 5, B_CONV = 7, B_Y = 10, B_ACC = 11, B_FREE = 12, B_FIN = 15, NBAR = 16 };
+__device__ __forceinline__ uint32_t par2(int c) { return (uint32_t)((c >> 1) & 1); }   // c-th use of a 2-ring
+__device__ __forceinline__ uint32_t par3(int c) { return (uint32_t)((c / 3) & 1); }    // c-th use of a 3-ring
 static_assert(TMAP_BOX_COLS == BLK && TMAP_BOX_ROWS == ROWS, "one TMA tile is one 128-row block of 32 columns");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert(NBAR * 8 + 16 <= BAR_BYTES, "barrier area");
 }  // namespace
 
 __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int j0, int nbp,
@@ -61,12 +70,11 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
     extern __shared__ unsigned char smem_raw[];
     char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     char* const AB = sm + OFF_AB;
-    char* const YJ = sm + OFF_YJ;
     char* const WD = sm + OFF_WD;
     char* const WT = sm + OFF_WT;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 128);
-    volatile int* err = reinterpret_cast<volatile int*>(sm + OFF_BAR + 132);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + NBAR * 8);
+    volatile int* err = reinterpret_cast<volatile int*>(sm + OFF_BAR + NBAR * 8 + 4);
 
     const int b = blockIdx.y;
     const int row0 = blockIdx.x * ROWS;
@@ -76,7 +84,8 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
 
     if (warp == 0) tc::tmem_alloc(tmem_slot, TCOLS);
     if (tid == 0) {
-        for (int i = 0; i < NBAR; ++i) tc::mbar_init(&bars[i], (i == B_CONV || i == B_CONV + 1 || i == B_Y) ? 128 : 1);
+        for (int i = 0; i < NBAR; ++i)
+            tc::mbar_init(&bars[i], ((i >= B_CONV && i < B_CONV + NSLOT) || i == B_Y) ? 128 : 1);
         tc::mbar_fence_init();
         *err = 0;
     }
@@ -123,10 +132,11 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
             tc::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) big[i] = __fadd_rn(big[i], small[i]);
-            if (j + 1 < nb) {   // Y_{j-1}'s update, which read the Y buffer, completed with acc[j]
+            if (j + 1 < nb) {   // Y_j into block j's slot: its operand was last read by diag(j), complete with acc[j]
+                char* slot = AB + (j % NSLOT) * SLOT;
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
-                    tc::store2_at(YJ, YJ + YT, tc::swz_off(me, q),
+                    tc::store2_at(slot, slot + YT, tc::swz_off(me, q),
                                   make_float4(big[4 * q], big[4 * q + 1], big[4 * q + 2], big[4 * q + 3]));
                 tc::fence_async_smem();
                 tc::mbar_arrive(&bars[B_Y]);
@@ -152,11 +162,11 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
         const int t = tid - 128, aq = t & 7, am = t >> 3;   // rows 16 i + am, k-quad aq
         // exits are decided by the whole group (bar_and): it meets again at a named barrier
         for (int c = 0; c < nb; ++c) {
-            if (!tc::bar_and(1, 128, !*err && tc::mbar_wait(&bars[B_A + (c & 1)], ring_parity(c)))) {
+            if (!tc::bar_and(1, 128, !*err && tc::mbar_wait(&bars[B_A + c % NSLOT], par3(c)))) {
                 *err = 1;
                 break;
             }
-            char* buf = AB + (c & 1) * 2 * YT;
+            char* buf = AB + (c % NSLOT) * SLOT;
             float4 v[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -178,7 +188,7 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
 #pragma unroll
             for (int i = 0; i < 8; ++i) tc::store2_at(buf, buf + YT, tc::swz_off(16 * i + am, aq), v[i]);
             tc::fence_async_smem();
-            tc::mbar_arrive(&bars[B_CONV + (c & 1)]);
+            tc::mbar_arrive(&bars[B_CONV + c % NSLOT]);
         }
     } else if (warp == 8) {
         // ---------------- product warp ----------------
@@ -196,31 +206,30 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
                     tc::mma_tf32(tmem + 256 + col, alo, bhi, idesc, 1u);
                 }
             };
-            auto diag_products = [&](int c) {   // acc[c] += A_c W_cc^T
-                const uint32_t a = tc::smem_u32(AB + (c & 1) * 2 * YT), w = tc::smem_u32(WD + (c & 1) * 2 * WPART);
-                products(32 * c, a, a + YT, w, w + WPART, BLK);
-            };
-            bool ok = tc::mbar_wait(&bars[B_CONV], 0u) && tc::mbar_wait(&bars[B_WD], 0u);
-            if (ok) {
+            auto diag = [&](int c) -> bool {   // acc[c] += A_c W_cc^T
+                if (*err || !tc::mbar_wait(&bars[B_CONV + c % NSLOT], par3(c)) || !tc::mbar_wait(&bars[B_WD + (c & 1)], par2(c)))
+                    return false;
                 tc::fence_after_sync();
-                diag_products(0);
-                tc::mma_commit(&bars[B_ACC]);
-            }
+                const uint32_t a = tc::smem_u32(AB + (c % NSLOT) * SLOT), w = tc::smem_u32(WD + (c & 1) * 2 * WPART);
+                products(32 * c, a, a + YT, w, w + WPART, BLK);
+                return true;
+            };
+            bool ok = diag(0);
+            if (ok) tc::mma_commit(&bars[B_ACC]);
             for (int j = 0; ok && j + 1 < nb; ++j) {
-                const int c = j + 1;
-                // Y_j is in shared memory (the epilogue read acc[j]: every product issued before has completed)
-                ok = !*err && tc::mbar_wait(&bars[B_CONV + (c & 1)], ring_parity(c)) &&
-                     tc::mbar_wait(&bars[B_WD + (c & 1)], ring_parity(c)) &&
-                     tc::mbar_wait(&bars[B_WT + (j & 1)], ring_parity(j)) &&
-                     tc::mbar_wait(&bars[B_Y], (uint32_t)(j & 1));
+                ok = diag(j + 1) && !*err && tc::mbar_wait(&bars[B_Y], (uint32_t)(j & 1)) &&
+                     tc::mbar_wait(&bars[B_WT + (j & 1)], par2(j));
                 if (!ok) break;
                 tc::fence_after_sync();
-                diag_products(c);   // acc[j+1] += A_{j+1} W_{j+1,j+1}^T
-                const uint32_t yj = tc::smem_u32(YJ), wt = tc::smem_u32(WT + (j & 1) * WTBUF);
-                // acc[j+1 ..] += Y_j W_{j+1 .., j}^T
-                products(32 * (j + 1), yj, yj + YT, wt, wt + (uint32_t)(nb - 1 - j) * WPART, BLK * (nb - 1 - j));
+                const int t = nb - 1 - j;   // trailing tiles of column j in this panel: blocks j + 1 .. nb - 1
+                const uint32_t yj = tc::smem_u32(AB + (j % NSLOT) * SLOT), wt = tc::smem_u32(WT + (j & 1) * WTBUF);
+                // T1: block j + 1, which is then complete
+                products(32 * (j + 1), yj, yj + YT, wt, wt + (uint32_t)t * WPART, BLK);
                 tc::mma_commit(&bars[B_ACC]);
-                tc::mma_commit(&bars[B_FREE]);
+                // T2: the later blocks, one product
+                if (t > 1)
+                    products(32 * (j + 2), yj, yj + YT, wt + WPART, wt + (uint32_t)(t + 1) * WPART, BLK * (t - 1));
+                tc::mma_commit(&bars[B_FREE + j % NSLOT]);
             }
             if (!ok) {
                 *err = 1;
@@ -234,14 +243,14 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
             const void* amap = maps + ((size_t)b * TMAPS_PER_MATRIX + (src == SRC_X ? TMAP_X : TMAP_Q)) * 128;
             const char* Wimg = W_all + (size_t)b * wcol_off(NB, NB);
             tc::tmap_acquire(amap);
-            int n_a[2] = {0, 0}, n_wd[2] = {0, 0}, n_wt[2] = {0, 0};
-            auto issue_a = [&](int c) {   // raw A_c into A buffer c % 2: x tile, and z tile behind it in the first pass
-                uint64_t* bar = &bars[B_A + (c & 1)];
-                char* dst = AB + (c & 1) * 2 * YT;
+            int n_a[NSLOT] = {0, 0, 0}, n_wd[2] = {0, 0}, n_wt[2] = {0, 0};
+            auto issue_a = [&](int c) {   // raw A_c into slot c % 3: x tile, and z tile behind it in the first pass
+                uint64_t* bar = &bars[B_A + c % NSLOT];
+                char* dst = AB + (c % NSLOT) * SLOT;
                 tc::mbar_expect_tx(bar, has_z ? 2 * YT : YT);
                 tc::tma_load_2d(dst, amap, (j0 + c) * BLK, row0, bar);
                 if (has_z) tc::tma_load_2d(dst + YT, &zmap, (j0 + c) * BLK, row0, bar);
-                ++n_a[c & 1];
+                ++n_a[c % NSLOT];
             };
             auto issue_wd = [&](int c) {
                 uint64_t* bar = &bars[B_WD + (c & 1)];
@@ -264,28 +273,29 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
                 ++n_wt[c & 1];
             };
             bool ok = true;
-            issue_a(0);
-            issue_wd(0);
-            if (nb > 1) {
-                issue_a(1);
-                issue_wd(1);
-                issue_wt(0);
+            for (int c = 0; c < nb && c < NSLOT; ++c) issue_a(c);
+            for (int c = 0; c < nb && c < 2; ++c) issue_wd(c);
+            for (int c = 0; c + 1 < nb && c < 2; ++c) issue_wt(c);
+            if (nb > 2) {   // diag(0) done: its tile's buffer takes W_22
+                ok = !*err && tc::mbar_wait(&bars[B_ACC], 0u);
+                if (ok) issue_wd(2);
             }
-            if (nb > 2) issue_wt(1);
-            for (int j = 0; j + 2 < nb; ++j) {
-                // phase j: Y_j's update (and block j's own product before it) completed, so block j's A buffer, its
-                // diagonal tile and its trailing W buffer are free; phase j + 1 needs A_{j+2}, issued below
-                ok = !*err && tc::mbar_wait(&bars[B_FREE], (uint32_t)(j & 1));
+            for (int j = 0; ok && j + 2 < nb; ++j) {
+                // slot j % 3 released: T1(j), T2(j) and diag(j + 1) (issued before them) are complete
+                ok = !*err && tc::mbar_wait(&bars[B_FREE + j % NSLOT], par3(j));
                 if (!ok) break;
-                issue_a(j + 2);
-                issue_wd(j + 2);
-                if (j + 2 <= nb - 2) issue_wt(j + 2);
+                if (j + 3 < nb) {
+                    issue_a(j + 3);    // into slot j % 3 (Y_j consumed)
+                    issue_wd(j + 3);   // into W_{j+1,j+1}'s buffer (diag(j + 1) done)
+                }
+                if (j + 2 <= nb - 2) issue_wt(j + 2);   // into column j's buffer
             }
             if (!ok) {
                 *err = 1;
                 // let issued copies finish before this CTA's shared memory is released
-                for (int i = 0; i < 2; ++i) {
+                for (int i = 0; i < NSLOT; ++i)
                     if (n_a[i]) tc::mbar_wait(&bars[B_A + i], (uint32_t)((n_a[i] - 1) & 1));
+                for (int i = 0; i < 2; ++i) {
                     if (n_wd[i]) tc::mbar_wait(&bars[B_WD + i], (uint32_t)((n_wd[i] - 1) & 1));
                     if (n_wt[i]) tc::mbar_wait(&bars[B_WT + i], (uint32_t)((n_wt[i] - 1) & 1));
                 }

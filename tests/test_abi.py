@@ -62,6 +62,16 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_gram_mode_f32(al, 64, 256, 64, None, 3, al, al, 10 ** 9, None) == ARG      # no such mode
     assert L.spanqr_gram_mode_f32(al, 64, 32, 64, None, 1, al, al, 10 ** 9, None) == SHAPE     # K < n
     assert L.spanqr_gram_mode_f32(al, 64, 256, 64, None, 2, al, al, ws_need - 1, None) == WS   # workspace too small
+    Ks = (ctypes.c_int * 3)(512, 256, 512)
+    n = ctypes.c_size_t(0)
+    assert L.spanqr_workspace_bytes_mixed(ctypes.cast(Ks, ctypes.c_void_p), 64, 3, ctypes.byref(n)) == OK
+    assert n.value >= _lib.workspace_bytes(512, 64, 2) + _lib.workspace_bytes(256, 64, 1)
+    assert L.spanqr_workspace_bytes_mixed(ctypes.cast(Ks, ctypes.c_void_p), 1024, 3, ctypes.byref(n)) == SHAPE
+    zs = (ctypes.c_void_p * 3)(al, al, al + 256)        # two dust pointers for the height 512
+    ps = (ctypes.c_void_p * 3)(al, al, al)
+    assert L.spanqr_orth_mixed_f32(ctypes.cast(ps, ctypes.c_void_p), ctypes.cast(ps, ctypes.c_void_p),
+                                   ctypes.cast(Ks, ctypes.c_void_p), 64, 3, ctypes.cast(zs, ctypes.c_void_p), al,
+                                   10 ** 9, None) == ARG
     h = ctypes.c_void_p()
     assert L.spanqr_orth_graph_create(256, 100, 100, 100, al, al, 10 ** 9, ctypes.byref(h)) == SHAPE
     assert L.spanqr_orth_graph_create(256, 64, 64, 64, al + 4, al, 10 ** 9, ctypes.byref(h)) == ARG   # misaligned Z

@@ -40,8 +40,27 @@ def test_borth_matches_oracle(K, r, kappa, deficient):
         assert np.abs(q - qo).max() <= elementwise_tol(_kappa(X))
 
 
+def test_width_above_512_not_a_multiple_of_256_is_padded():
+    """r in (512, 1024] that is not a multiple of 256 (the reference runs kcholqr_f there, orth.py:18-20): zero columns
+    up to the next multiple of 256, blockwise, the first r columns returned; equal to the oracle's borth on the padded
+    matrix within the elementwise bound, orthonormal and spanning X"""
+    K, r, rp = 2048, 640, 768
+    X = (_mixed(K, r, 1e3, 13) * 4.0).astype(np.float32)
+    Q = orth(torch.from_numpy(X).cuda())
+    torch.cuda.synchronize()
+    assert Q.shape == (K, r)
+    q = Q.cpu().numpy().astype(np.float64)
+    Xp = np.zeros((K, rp), np.float32)
+    Xp[:, :r] = X
+    qo = oracle.borth(Xp, zdust(K, rp, "cuda").cpu().numpy())[:, :r]
+    assert np.abs(q - qo).max() <= elementwise_tol(_kappa(X))
+    assert np.abs(q.T @ q - np.eye(r)).max() <= 2e-7
+    Xd = X.astype(np.float64)
+    assert np.linalg.norm(Xd - q @ (q.T @ Xd)) <= 1e-5 * np.linalg.norm(Xd)
+
+
 def test_borth_rejects_what_the_block_path_cannot_take():
     with pytest.raises(ValueError):
-        orth(torch.zeros(2048, 640, device="cuda"))   # r > 512, not a multiple of 256
-    with pytest.raises(ValueError):
         orth(torch.zeros(700, 768, device="cuda"))    # K < r
+    with pytest.raises(ValueError):
+        orth(torch.zeros(700, 640, device="cuda"))    # r 640 is padded to 768 > K

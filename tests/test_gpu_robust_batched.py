@@ -76,6 +76,30 @@ def test_batched_mixed_shapes():
         assert q.shape == x.shape and _bits(q, orth(x))
 
 
+def test_mixed_height_entry_point():
+    """spanqr_orth_mixed_f32: one call over matrices of two heights, interleaved; each gets its lone orth bits"""
+    import ctypes
+    r = 256
+    Xs = [cases.cfg3_matrix(i, K=(1024 if i % 2 else 640), r=r).cuda() for i in range(7)]
+    want = [orth(x) for x in Xs]
+    Qs = [torch.empty_like(x) for x in Xs]
+    B = len(Xs)
+    Ks = (ctypes.c_int * B)(*[x.shape[0] for x in Xs])
+    Zs = [zdust(x.shape[0], r, x.device) for x in Xs]
+    P = ctypes.c_void_p * B
+    hx, hq, hz = P(*[x.data_ptr() for x in Xs]), P(*[q.data_ptr() for q in Qs]), P(*[z.data_ptr() for z in Zs])
+    need = ctypes.c_size_t(0)
+    L = _lib.lib()
+    _lib.check(L.spanqr_workspace_bytes_mixed(ctypes.cast(Ks, ctypes.c_void_p), r, B, ctypes.byref(need)), "ws")
+    assert need.value >= _lib.workspace_bytes(1024, r, 3) + _lib.workspace_bytes(640, r, 4)
+    ws = torch.empty(need.value, dtype=torch.uint8, device="cuda")
+    _lib.check(L.spanqr_orth_mixed_f32(ctypes.cast(hx, ctypes.c_void_p), ctypes.cast(hq, ctypes.c_void_p),
+                                       ctypes.cast(Ks, ctypes.c_void_p), r, B, ctypes.cast(hz, ctypes.c_void_p),
+                                       ws.data_ptr(), ws.numel(), torch.cuda.current_stream().cuda_stream), "mixed")
+    torch.cuda.synchronize()
+    assert all(_bits(q, w) for q, w in zip(Qs, want))
+
+
 def test_strided_and_device_pointer_entry_points():
     B, K, r = 4, 512, 128
     X = torch.stack([cases.cfg3_matrix(i, K=K, r=r) for i in range(B)]).cuda()

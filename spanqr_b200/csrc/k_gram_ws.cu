@@ -25,22 +25,25 @@ constexpr int RAWB = GRAM_BOX_COLS * CH * 4; // one raw box: 128 columns x 32 ro
 constexpr int RAW_STAGE = 2 * RAWB;          // up to two boxes (256 columns)
 constexpr int OP_PART = 256 * CH * 4;        // one operand part (hi or lo) of up to 256 columns: 32 KB
 constexpr int OP_STAGE = 2 * OP_PART;
-constexpr int STAGES = 2;
+constexpr int RSTAGES = 3;                   // raw chunks in flight (copies three chunks ahead of the conversion)
+constexpr int OSTAGES = 2;                   // operand chunks
 constexpr int OFF_RAW = 0;
-constexpr int OFF_OP = OFF_RAW + STAGES * RAW_STAGE;
-constexpr int OFF_DSQ = OFF_OP + STAGES * OP_STAGE;  // 4 convert warps x 128 columns of fp64 squares
-constexpr int OFF_BAR = OFF_DSQ + 4 * TILE * 8;
+constexpr int OFF_OP = OFF_RAW + RSTAGES * RAW_STAGE;
+constexpr int OFF_DSQ = OFF_RAW;             // after the last chunk: 4 convert warps x 128 columns of fp64 squares
+constexpr int OFF_BAR = OFF_OP + OSTAGES * OP_STAGE;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TCOLS = 512;              // large at 0, small at 256
 constexpr int ERR_TIMEOUT = 0x10;
 // mbarriers (per stage where doubled): raw chunk landed, raw chunk read (128 arrivals), operands written (128
 // arrivals), operands consumed, all products done, error drain.  Every waiter steps through a barrier's phases in
 // order from phase 0, and no barrier can run two phases ahead of a waiter.
-enum { B_RAW = 0, B_RAWFREE = 2, B_OP = 4, B_OPFREE = 6, B_DONE = 8, B_FIN = 9, NBAR = 10 };
+enum { B_RAW = 0, B_RAWFREE = 3, B_OP = 6, B_OPFREE = 8, B_DONE = 10, B_FIN = 11, NBAR = 12 };
+static_assert(4 * TILE * 8 <= RAW_STAGE, "the squares fit one raw stage");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 static_assert(GRAM_BOX_ROWS == CH && GRAM_BOX_COLS == TILE, "one TMA box is 128 columns of one chunk");
 
-__device__ __forceinline__ uint32_t ring_parity(int c) { return (uint32_t)((c >> 1) & 1); }
+__device__ __forceinline__ uint32_t ring_parity(int c) { return (uint32_t)((c >> 1) & 1); }   // c-th use of a 2-ring
+__device__ __forceinline__ uint32_t par3(int c) { return (uint32_t)((c / 3) & 1); }            // c-th use of a 3-ring
 
 // byte offset of (k, mn .. mn+3) in an operand part whose MN extent is `w` (a multiple of 128): 32-byte-base layout,
 // atoms of 4 k-rows x 32 MN (512 bytes) with the 32-byte granule g of k-row r at granule position g ^ r, MN-atoms
@@ -75,7 +78,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
     if (warp == 0) tc::tmem_alloc(tmem_slot, TCOLS);
     if (tid == 0) {
         for (int i = 0; i < NBAR; ++i)
-            tc::mbar_init(&bars[i], (i >= B_RAWFREE && i < B_OPFREE) ? 128 : 1);
+            tc::mbar_init(&bars[i], (i >= B_RAWFREE && i < B_OPFREE) ? 128 : 1);   // raw read, operands written
         tc::mbar_fence_init();
         *err = 0;
     }
@@ -131,12 +134,12 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
         const int cw = warp - 4;
         double dsq[4] = {0.0, 0.0, 0.0, 0.0};   // squares of panel columns 4 lane .. 4 lane + 3
         for (int c = 0; c < nchunks; ++c) {
-            const int st = c & 1;
-            if (*err || !tc::mbar_wait(&bars[B_RAW + st], ring_parity(c))) {
+            const int st = c & 1, rs = c % RSTAGES;
+            if (*err || !tc::mbar_wait(&bars[B_RAW + rs], par3(c))) {
                 *err = 1;
                 break;
             }
-            const char* raw = RAW + st * RAW_STAGE;
+            const char* raw = RAW + rs * RAW_STAGE;
             float4 v[2][8];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -147,9 +150,9 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                 }
             }
             // the next TMA load into this stage writes through the async proxy: the generic reads above must be
-            // ordered before it by a proxy fence (without it, bytes of chunk c + 2 were seen in place of chunk c's)
+            // ordered before it by a proxy fence (without it, bytes of a later chunk were seen in place of chunk c's)
             tc::fence_async_smem();
-            tc::mbar_arrive(&bars[B_RAWFREE + st]);
+            tc::mbar_arrive(&bars[B_RAWFREE + rs]);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 float4& x = v[0][i];
@@ -183,6 +186,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
             tc::fence_async_smem();
             tc::mbar_arrive(&bars[B_OP + st]);
         }
+        tc::bar_sync(1, 128);   // every convert warp is done with the raw stages: the squares go into the first one
 #pragma unroll
         for (int j = 0; j < 4; ++j) DSQ[cw * TILE + 4 * lane + j] = dsq[j];
         tc::bar_sync(3, 256);
@@ -222,22 +226,22 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
         if (lane == 0) {
             const void* map = maps + ((size_t)b * TMAPS_PER_MATRIX + (src == SRC_X ? TMAP_GX : TMAP_GQ)) * 128;
             tc::tmap_acquire(map);
-            int issued[2] = {0, 0};
+            int issued[RSTAGES] = {0, 0, 0};
             bool ok = true;
             for (int c = 0; c < nchunks; ++c) {
-                const int st = c & 1;
-                if (c >= 2) {
-                    ok = !*err && tc::mbar_wait_sleep(&bars[B_RAWFREE + st], ring_parity(c - 2), 100);   // c - 2 read
+                const int rs = c % RSTAGES;
+                if (c >= RSTAGES) {
+                    ok = !*err && tc::mbar_wait_sleep(&bars[B_RAWFREE + rs], par3(c - RSTAGES), 100);   // c - 3 read
                     if (!ok) break;
                 }
-                tc::mbar_expect_tx(&bars[B_RAW + st], (uint32_t)(nbox * RAWB));
+                tc::mbar_expect_tx(&bars[B_RAW + rs], (uint32_t)(nbox * RAWB));
                 for (int h = 0; h < nbox; ++h)
-                    tc::tma_load_2d(RAW + st * RAW_STAGE + h * RAWB, map, col0 + h * TILE, k0 + c * CH, &bars[B_RAW + st]);
-                ++issued[st];
+                    tc::tma_load_2d(RAW + rs * RAW_STAGE + h * RAWB, map, col0 + h * TILE, k0 + c * CH, &bars[B_RAW + rs]);
+                ++issued[rs];
             }
             if (!ok) {
                 *err = 1;
-                for (int i = 0; i < 2; ++i)   // let issued copies land before the shared memory is released
+                for (int i = 0; i < RSTAGES; ++i)   // let issued copies land before the shared memory is released
                     if (issued[i]) tc::mbar_wait(&bars[B_RAW + i], (uint32_t)((issued[i] - 1) & 1));
             }
         }

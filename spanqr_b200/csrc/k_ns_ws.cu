@@ -94,16 +94,26 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
         float* qr = (p.tab ? p.tab[b] : p.one).Q + (long long)row * ldq;
         float* sr = scratch ? scratch + ((size_t)b * K + (size_t)(row < K ? row : 0)) * 256 : nullptr;
         const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+        // the addend y (this row of Q before the update; nothing writes it before the last half's epilogue) is loaded
+        // one 32-column block ahead: the first before the products are done, each next one during the current one
+        const bool addend = MODE == 0 && row < K;
+        float4 yv[8], yn[8];
+        auto load_y = [&](float4 (&y)[8], int col) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) y[i] = addend ? *reinterpret_cast<const float4*>(qr + col + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        };
         for (int h = 0; h < nh; ++h) {
+            const int c0 = h * N;
+            load_y(yv, c0);
             const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], (uint32_t)(h & 1), 500);
             if (!__all_sync(0xffffffffu, done && !*err)) {   // per warp: tcgen05.ld needs the whole warp
                 *err = 1;
                 break;
             }
             tc::fence_after_sync();
-            const int c0 = h * N;
             float* dst = (MODE == 1 || (nh > 1 && h + 1 < nh)) ? sr : qr + c0;   // an earlier half waits in scratch
             for (int cb = 0; cb < N / 32; ++cb) {
+                if (cb + 1 < N / 32) load_y(yn, c0 + 32 * (cb + 1));
                 float big[32], small[32];
                 tc::tmem_ld32(tl + 32 * cb, big);
                 tc::tmem_ld32(tl + 256 + 32 * cb, small);
@@ -117,7 +127,7 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                 } else if (row < K) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 4) {
-                        float4 y = *reinterpret_cast<const float4*>(qr + c0 + 32 * cb + i);
+                        float4 y = yv[i / 4];
                         y.x = __fadd_rn(y.x, __fadd_rn(big[i], small[i]));
                         y.y = __fadd_rn(y.y, __fadd_rn(big[i + 1], small[i + 1]));
                         y.z = __fadd_rn(y.z, __fadd_rn(big[i + 2], small[i + 2]));
@@ -125,6 +135,8 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                         *reinterpret_cast<float4*>(dst + 32 * cb + i) = y;
                     }
                 }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) yv[i] = yn[i];
             }
             if (nh > 1 && h + 1 < nh) {   // the next half's products may overwrite the accumulators
                 tc::fence_before_sync();

@@ -63,6 +63,35 @@ __device__ __forceinline__ void cluster_sync_all() {
 
 __host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// Float-float accumulation (Knuth's two-sum; the square's rounding error from a fused multiply-add): a sum kept as
+// hi + lo in two fp32 registers, about 44 significant bits, at the full fp32 rate.  B200 converts fp32 to fp64 at
+// about a tenth of its fp64 add rate, so sums of fp32 terms that need more than fp32 accuracy are kept this way and
+// converted to fp64 once, at the end.  Every operation is explicitly rounded (no contraction), so the order of the
+// terms alone decides the result.
+__device__ __forceinline__ void two_sum(float a, float b, float& s, float& e) {
+    s = __fadd_rn(a, b);
+    const float bb = __fsub_rn(s, a);
+    e = __fadd_rn(__fsub_rn(a, __fsub_rn(s, bb)), __fsub_rn(b, bb));
+}
+// (hi, lo) += x
+__device__ __forceinline__ void ff_add(float& hi, float& lo, float x) {
+    float s, e;
+    two_sum(hi, x, s, e);
+    hi = s;
+    lo = __fadd_rn(lo, e);
+}
+// (hi, lo) += x * x, the product split exactly into its rounded value and its error
+__device__ __forceinline__ void ff_add_sq(float& hi, float& lo, float x) {
+    const float p = __fmul_rn(x, x);
+    const float pe = __fmaf_rn(x, x, -p);
+    float s, e;
+    two_sum(hi, p, s, e);
+    hi = s;
+    lo = __fadd_rn(lo, __fadd_rn(e, pe));
+}
+// the float-float value in fp64
+__device__ __forceinline__ double ff_value(float hi, float lo) { return __dadd_rn((double)hi, (double)lo); }
+
 // upper-triangular tile index -> (ti, tj) with ti <= tj, row-major over the upper triangle of nt x nt tiles
 __device__ __forceinline__ void upper_tile(int t, int nt, int& ti, int& tj) {
     ti = 0;

@@ -1,7 +1,8 @@
 // The Gram's fixed-order reduction over splits.
 //
-// k_gram_reduce: G = fp64 sum of the split partials of k_gram_tc (128 x 128 tiles of the upper triangle) in split
-// order, rounded to fp32 and mirrored, as tri.py:375 sums its splits (P.sum(0, float64).float()); with make_D it
+// k_gram_reduce: G = the sum of the split partials of k_gram_tc (128 x 128 tiles of the upper triangle) in split
+// order, kept in float-float (about 44 bits, where tri.py:375 sums its splits in fp64: P.sum(0, float64).float()),
+// rounded to fp32 once and mirrored; with make_D it
 // writes D = 0.5 (I - G) instead (kcholqr.py:21).  Without make_D it also writes, per strip, the fp64 sum of the
 // squares of the G entries it wrote (every entry of G is written exactly once): the Cholesky adds these partial sums
 // in a fixed order for ||G||_F (kcholqr.py:107).
@@ -28,8 +29,8 @@ __global__ void __launch_bounds__(256) k_gram_reduce(const float* __restrict__ P
     // 32 x 128 sums, a float4 of one row per thread and step
     for (int q = threadIdx.x; q < RSTRIP * T / 4; q += blockDim.x) {
         const int r = q / (T / 4), c = 4 * (q % (T / 4));
-        double t0 = 0.0, t1 = 0.0, t2 = 0.0, t3 = 0.0;
-        // eight splits' loads in flight at a time; the sums still run in split order
+        // float-float sums (B200 converts fp32 to fp64 slowly), eight splits' loads in flight at a time, split order
+        float h[4] = {0.f, 0.f, 0.f, 0.f}, l[4] = {0.f, 0.f, 0.f, 0.f};
         for (int sp0 = 0; sp0 < gp.S; sp0 += 8) {
             float4 v[8];
 #pragma unroll
@@ -39,12 +40,14 @@ __global__ void __launch_bounds__(256) k_gram_reduce(const float* __restrict__ P
 #pragma unroll
             for (int u = 0; u < 8; ++u)
                 if (sp0 + u < gp.S) {
-                    t0 = __dadd_rn(t0, (double)v[u].x);
-                    t1 = __dadd_rn(t1, (double)v[u].y);
-                    t2 = __dadd_rn(t2, (double)v[u].z);
-                    t3 = __dadd_rn(t3, (double)v[u].w);
+                    ff_add(h[0], l[0], v[u].x);
+                    ff_add(h[1], l[1], v[u].y);
+                    ff_add(h[2], l[2], v[u].z);
+                    ff_add(h[3], l[3], v[u].w);
                 }
         }
+        const double t0 = ff_value(h[0], l[0]), t1 = ff_value(h[1], l[1]), t2 = ff_value(h[2], l[2]),
+                     t3 = ff_value(h[3], l[3]);
         const int a = ti * T + r0 + r;
         float g[4] = {__double2float_rn(t0), __double2float_rn(t1), __double2float_rn(t2), __double2float_rn(t3)};
 #pragma unroll

@@ -11,20 +11,22 @@
 // hi.hi goes to one TMEM accumulator and the small products to a second one, so the small terms never round
 // against the large partial sum.  After every group of rows the large-term accumulator is drained into fp64 registers
 // while the next group accumulates in the other TMEM buffer; the small-term accumulator (about 2^-11 of the total) stays in
-// TMEM for the whole split and is drained once at the end.  The split's fp64 sum is rounded to fp32 and written as
-// a partial.  k_gram_reduce (k_gram.cu) sums the partials in split order in fp64.  Which mode runs where: the orth
+// TMEM for the whole split and is drained once at the end.  The split's fp64 sum is rounded to fp32 and written as a
+// partial.  k_gram_reduce
+// (k_gram.cu) sums the partials in split order.  Which mode runs where: the orth
 // sequence uses the drained mode for its last polish Gram (the reference's compensated gram_split, kcholqr.py:20) and
 // the plain mode for the Grams of r > 256 (k_gram_ws covers r <= 256); the accurate mode serves the component entry
 // point spanqr_gram_f32, the counterpart of the reference's compensated gram_f / gram_split (tri.py:285-375).
 // Determinism: the split size (512 rows) and every order depend only on (K, n), never on the batch or the GPU.
 // Compensation: the reference (candidates/tri.py:255-375) Kahan-sums fp32 32-row dots inside a split and adds the
-// splits in fp64; here each group of rows (32 in the accurate mode, 128 in the plain mode) sums its products in the
+// splits in fp64; here each group of rows (32 in the accurate mode, 128 in the drained mode) sums its products in the
 // tensor core's fp32 and the groups are added in fp64.
 // The tensor core's fp32 accumulation rounds toward zero, so a sum of same-sign products drifts low by about half
 // an ulp per accumulation (measured: -19 ulps of sum |y_i y_j| after 128 rows on the diagonal, under 2.3 ulps off the
 // diagonal of an orthonormal Y).  The diagonal -- every column's sum of squares, the entries that set the final
-// orthogonality -- is therefore computed on the CUDA cores in fp64 from the same scaled values (exact squares,
-// fixed-order sums) by the diagonal-tile CTAs and written over the tensor-core diagonal.
+// orthogonality -- is therefore computed on the CUDA cores from the same scaled values (squares split exactly into
+// value and error, float-float sums in a fixed order) by the diagonal-tile CTAs and written over the tensor-core
+// diagonal.
 #include "kernels.h"
 #include "tc.cuh"
 
@@ -123,16 +125,16 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
             rb[i] = vb;
         }
     };
-    double dsq[4] = {0.0, 0.0, 0.0, 0.0};   // diagonal tiles: sums of squares of columns colA .. colA + 3
+    float sqh[4] = {0.f, 0.f, 0.f, 0.f}, sql[4] = {0.f, 0.f, 0.f, 0.f};   // diagonal tiles: squares of colA .. + 3
     auto stage = [&](int bi, const float4 (&ra)[4], const float4 (&rb)[4]) {
         char* base = buf0 + bi * BUF;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             if (diag) {
-                dsq[0] = __fma_rn((double)ra[i].x, (double)ra[i].x, dsq[0]);
-                dsq[1] = __fma_rn((double)ra[i].y, (double)ra[i].y, dsq[1]);
-                dsq[2] = __fma_rn((double)ra[i].z, (double)ra[i].z, dsq[2]);
-                dsq[3] = __fma_rn((double)ra[i].w, (double)ra[i].w, dsq[3]);
+                ff_add_sq(sqh[0], sql[0], ra[i].x);
+                ff_add_sq(sqh[1], sql[1], ra[i].y);
+                ff_add_sq(sqh[2], sql[2], ra[i].z);
+                ff_add_sq(sqh[3], sql[3], ra[i].w);
             }
             if constexpr (PARTS == 2) tc::store2_at(base, base + OPND, soff[i], ra[i]);
             else tc::store3_at(base, base + OPND, base + 2 * OPND, soff[i], ra[i]);
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
             // diagonal of the partial tile
             double* dsum = reinterpret_cast<double*>(buf0);   // operand buffers are free: every MMA has completed
 #pragma unroll
-            for (int j = 0; j < 4; ++j) dsum[warp * TILE + 4 * lane + j] = dsq[j];
+            for (int j = 0; j < 4; ++j) dsum[warp * TILE + 4 * lane + j] = ff_value(sqh[j], sql[j]);
             __syncthreads();
             if (threadIdx.x < TILE) {
                 const int m = threadIdx.x;
@@ -335,7 +337,7 @@ __global__ void __launch_bounds__(PLAIN_NT, 2) k_gram_tc_plain(PtrArg p, Src src
             rb[i] = vb;
         }
     };
-    double dsq[4] = {0.0, 0.0, 0.0, 0.0};
+    float sqh[4] = {0.f, 0.f, 0.f, 0.f}, sql[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     load(0);
     for (int c = 0; c < nchunks; ++c) {
@@ -345,10 +347,10 @@ __global__ void __launch_bounds__(PLAIN_NT, 2) k_gram_tc_plain(PtrArg p, Src src
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             if (diag) {
-                dsq[0] = __fma_rn((double)ra[i].x, (double)ra[i].x, dsq[0]);
-                dsq[1] = __fma_rn((double)ra[i].y, (double)ra[i].y, dsq[1]);
-                dsq[2] = __fma_rn((double)ra[i].z, (double)ra[i].z, dsq[2]);
-                dsq[3] = __fma_rn((double)ra[i].w, (double)ra[i].w, dsq[3]);
+                ff_add_sq(sqh[0], sql[0], ra[i].x);
+                ff_add_sq(sqh[1], sql[1], ra[i].y);
+                ff_add_sq(sqh[2], sql[2], ra[i].z);
+                ff_add_sq(sqh[3], sql[3], ra[i].w);
             }
             tc::store2_at(buf, buf + OPND, soff[i], ra[i]);
             if (!diag) tc::store2_at(buf + 2 * OPND, buf + 3 * OPND, soff[i], rb[i]);
@@ -395,7 +397,7 @@ __global__ void __launch_bounds__(PLAIN_NT, 2) k_gram_tc_plain(PtrArg p, Src src
         if (diag) {
             double* dsum = reinterpret_cast<double*>(buf);   // operand buffer is free: every MMA has completed
 #pragma unroll
-            for (int j = 0; j < 4; ++j) dsum[warp * TILE + 4 * lane + j] = dsq[j];
+            for (int j = 0; j < 4; ++j) dsum[warp * TILE + 4 * lane + j] = ff_value(sqh[j], sql[j]);
             __syncthreads();
             if (threadIdx.x < TILE) {
                 const int m = threadIdx.x;

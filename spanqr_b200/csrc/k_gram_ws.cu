@@ -9,8 +9,9 @@
 // columns of B (columns 128 i .. n of Y), so one staged chunk of 32 rows serves both operands, MN-major in the 32-byte
 // base 128B-swizzled layout tcgen05 takes for 32-bit types.  The split accumulates in TMEM (hi.hi and the cross terms
 // in separate accumulators) and is written to the partial tiles P[b][split][tile] of k_gram_tc (the same layout, so
-// k_gram_reduce sums them unchanged); the tile diagonal is replaced by the exact fp64 sum of squares.
-// Warp roles: 0-3 epilogue (TMEM lanes = the panel's columns), 4-7 convert (raw chunk -> s y -> tf32 hi | lo, fp64
+// k_gram_reduce sums them unchanged); the tile diagonal is replaced by the sum of squares kept in float-float (exact
+// squares, about 44 bits).
+// Warp roles: 0-3 epilogue (TMEM lanes = the panel's columns), 4-7 convert (raw chunk -> s y -> tf32 hi | lo, float-float
 // squares of the panel's columns), 8 products (one thread), 9 copies (one thread, TMA through the per-matrix maps).
 #include "kernels.h"
 #include "tc.cuh"
@@ -29,7 +30,7 @@ constexpr int RSTAGES = 3;                   // raw chunks in flight (copies thr
 constexpr int OSTAGES = 2;                   // operand chunks
 constexpr int OFF_RAW = 0;
 constexpr int OFF_OP = OFF_RAW + RSTAGES * RAW_STAGE;
-constexpr int OFF_DSQ = OFF_RAW;             // after the last chunk: 4 convert warps x 128 columns of fp64 squares
+constexpr int OFF_DSQ = OFF_RAW;             // after the last chunk: 4 convert warps x 128 columns of squares (hi, lo)
 constexpr int OFF_BAR = OFF_OP + OSTAGES * OP_STAGE;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TCOLS = 512;              // large at 0, small at 256
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
     char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     char* const RAW = sm + OFF_RAW;
     char* const OP = sm + OFF_OP;
-    double* const DSQ = reinterpret_cast<double*>(sm + OFF_DSQ);
+    float2* const DSQ = reinterpret_cast<float2*>(sm + OFF_DSQ);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + 128);
     volatile int* err = reinterpret_cast<volatile int*>(sm + OFF_BAR + 132);
@@ -90,14 +91,14 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
     if (warp < 4) {
         // ---------------- epilogue: row a of tile row-panel pi (TMEM lane a) ----------------
         const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], 0u, 500);   // the whole split: sleep
-        tc::bar_sync(3, 256);   // the convert warps' fp64 squares are in shared memory
+        tc::bar_sync(3, 256);   // the convert warps' squares are in shared memory
         // decided per warp: tcgen05.ld needs the whole warp
         if (__all_sync(0xffffffffu, done && !*err)) {
             tc::fence_after_sync();
             const int a = warp * 32 + lane;
             double d = 0.0;
 #pragma unroll
-            for (int w = 0; w < 4; ++w) d = __dadd_rn(d, DSQ[w * TILE + a]);
+            for (int w = 0; w < 4; ++w) d = __dadd_rn(d, ff_value(DSQ[w * TILE + a].x, DSQ[w * TILE + a].y));
             const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
             float* Pb = P + (size_t)(b * gp.S + sp) * gp.tiles * TILE * TILE;
             for (int cb = 0; cb < W / 32; ++cb) {
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
             scaled = true;
         }
         const int cw = warp - 4;
-        double dsq[4] = {0.0, 0.0, 0.0, 0.0};   // squares of panel columns 4 lane .. 4 lane + 3
+        float sqh[4] = {0.f, 0.f, 0.f, 0.f}, sql[4] = {0.f, 0.f, 0.f, 0.f};   // squares of columns 4 lane .. + 3
         for (int c = 0; c < nchunks; ++c) {
             const int st = c & 1, rs = c % RSTAGES;
             if (*err || !tc::mbar_wait(&bars[B_RAW + rs], par3(c))) {
@@ -149,20 +150,19 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                         v[h][i] = *reinterpret_cast<const float4*>(raw + h * RAWB + (8 * cw + i) * 512 + 16 * lane);
                 }
             }
-            // the next TMA load into this stage writes through the async proxy: the generic reads above must be
-            // ordered before it by a proxy fence (without it, bytes of a later chunk were seen in place of chunk c's)
-            tc::fence_async_smem();
-            tc::mbar_arrive(&bars[B_RAWFREE + rs]);
+            // the raw stage is released after the one proxy fence below: the next TMA load into it writes through the
+            // async proxy, so these generic reads must be ordered before it by that fence (without one, bytes of a
+            // later chunk were seen in place of chunk c's)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 float4& x = v[0][i];
                 if (scaled) {
                     x.x = __fmul_rn(x.x, s); x.y = __fmul_rn(x.y, s); x.z = __fmul_rn(x.z, s); x.w = __fmul_rn(x.w, s);
                 }
-                dsq[0] = __fma_rn((double)x.x, (double)x.x, dsq[0]);
-                dsq[1] = __fma_rn((double)x.y, (double)x.y, dsq[1]);
-                dsq[2] = __fma_rn((double)x.z, (double)x.z, dsq[2]);
-                dsq[3] = __fma_rn((double)x.w, (double)x.w, dsq[3]);
+                ff_add_sq(sqh[0], sql[0], x.x);
+                ff_add_sq(sqh[1], sql[1], x.y);
+                ff_add_sq(sqh[2], sql[2], x.z);
+                ff_add_sq(sqh[3], sql[3], x.w);
                 if (nbox == 2 && scaled) {
                     float4& y = v[1][i];
                     y.x = __fmul_rn(y.x, s); y.y = __fmul_rn(y.y, s); y.z = __fmul_rn(y.z, s); y.w = __fmul_rn(y.w, s);
@@ -184,11 +184,12 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                 }
             }
             tc::fence_async_smem();
+            tc::mbar_arrive(&bars[B_RAWFREE + rs]);
             tc::mbar_arrive(&bars[B_OP + st]);
         }
         tc::bar_sync(1, 128);   // every convert warp is done with the raw stages: the squares go into the first one
 #pragma unroll
-        for (int j = 0; j < 4; ++j) DSQ[cw * TILE + 4 * lane + j] = dsq[j];
+        for (int j = 0; j < 4; ++j) DSQ[cw * TILE + 4 * lane + j] = make_float2(sqh[j], sql[j]);
         tc::bar_sync(3, 256);
     } else if (warp == 8) {
         // ---------------- products ----------------
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
             bool ok = true;
             for (int c = 0; c < nchunks; ++c) {
                 const int st = c & 1;
-                ok = !*err && tc::mbar_wait_sleep(&bars[B_OP + st], ring_parity(c), 20);
+                ok = !*err && tc::mbar_wait(&bars[B_OP + st], ring_parity(c));   // spin: this wait is the critical path
                 if (!ok) break;
                 tc::fence_after_sync();
                 const uint32_t hi = tc::smem_u32(OP + st * OP_STAGE), lo = hi + OP_PART;

@@ -181,10 +181,11 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
             for (int g = 0; g < total; ++g) {
                 const int st = g & 1, h = (nh > 1 && g >= nchunks) ? 1 : 0, c = g - h * nchunks;
                 if (nh > 1 && c == 0 && h > 0) {   // the previous half's accumulators have been read
-                    ok = !*err && tc::mbar_wait_sleep(&bars[B_TFREE], (uint32_t)((h - 1) & 1), 20);
+                    ok = !*err && tc::mbar_wait(&bars[B_TFREE], (uint32_t)((h - 1) & 1));
                     if (!ok) break;
                 }
-                ok = !*err && tc::mbar_wait_sleep(&bars[B_OP + st], ring_parity(g), 20) &&
+                ok = !*err && tc::mbar_wait(&bars[B_OP + st], ring_parity(g)) &&   // spin: the critical path
+                     
                      tc::mbar_wait(&bars[B_D + st], ring_parity(g));
                 if (!ok) break;
                 tc::fence_after_sync();

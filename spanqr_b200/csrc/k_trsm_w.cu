@@ -28,11 +28,12 @@ __global__ void __launch_bounds__(256) k_trsm_w(const float* __restrict__ L_all,
         hi = col + 2 * 4096 + (size_t)(j - k - 1) * 4096;
         lo = hi + (size_t)(nb - 1 - k) * 4096;
     }
-    __shared__ float sLi[TB][TB + 1], sL[TB][TB + 1];
+    // the tiles in fp64, converted once (B200 converts fp32 to fp64 at a tenth of its fp64 fma rate)
+    __shared__ double sLi[TB][TB + 1], sL[TB][TB + 1];
     for (int e = threadIdx.x; e < TB * TB; e += blockDim.x) {
         const int r = e / TB, c = e % TB;
-        sLi[r][c] = Li[(size_t)(j * TB + r) * TB + c];
-        sL[r][c] = (k < j) ? L[(size_t)(j * TB + r) * n + k * TB + c] : 0.0f;
+        sLi[r][c] = (double)Li[(size_t)(j * TB + r) * TB + c];
+        sL[r][c] = (k < j) ? (double)L[(size_t)(j * TB + r) * n + k * TB + c] : 0.0;
     }
     __syncthreads();
     // thread: row r, columns 4 q .. 4 q + 3 (q = 0..7)
@@ -42,11 +43,11 @@ __global__ void __launch_bounds__(256) k_trsm_w(const float* __restrict__ L_all,
     for (int i = 0; i < 4; ++i) {
         const int c = 4 * q + i;
         if (k == j) {
-            w[i] = sLi[r][c];
+            w[i] = (float)sLi[r][c];
         } else {
             double acc = 0.0;
 #pragma unroll 8
-            for (int m = 0; m < TB; ++m) acc = __fma_rn((double)sLi[r][m], (double)sL[m][c], acc);
+            for (int m = 0; m < TB; ++m) acc = __fma_rn(sLi[r][m], sL[m][c], acc);
             w[i] = -__double2float_rn(acc);
         }
     }

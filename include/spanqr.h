@@ -21,6 +21,7 @@
  *   spanqr_orth_ptrs_f32     no reference counterpart: same, from host arrays of matrix pointers
  *   spanqr_orth_graph_*      no reference counterpart: spanqr_orth_f32 captured once per shape, replayed per call
  *   spanqr_orth_mixed_f32    no reference counterpart: a batch of layers of one width and different heights
+ *   spanqr_borth_f32         orth.py:18-19 -> candidates/kbig.py:66-95 borth(X, b=256) (r > 512)
  *   spanqr_gram_f32          candidates/tri.py:362-375 gram_f(Y, s) and tri.py:285-297 gram_split(Y, bt=64)
  *   spanqr_gram_mode_f32     the same, and kcholqr.py:106 Y.T @ Y (each Gram of the orth sequence on its own)
  *   spanqr_chol_f32          candidates/kchol.py:35-44 chol32(G, tau) (kernel candidates/cuk/chol.cu:273-276)
@@ -93,6 +94,19 @@ int spanqr_orth_ptrs_f32(const float* const* hX, float* const* hQ, int K, int r,
 int spanqr_workspace_bytes_mixed(const int* K, int r, int batch, size_t* bytes);
 int spanqr_orth_mixed_f32(const float* const* hX, float* const* hQ, const int* K, int r, int batch,
                           const float* const* Z, void* ws, size_t ws_bytes, spanqr_stream_t stream);
+
+/*
+ * Q = borth(X) for r > 512 (orth.py:18-19 -> candidates/kbig.py:66-95, block Gram-Schmidt with reorthogonalisation
+ * over 256-column blocks, every Cholesky 256 wide): X, Q fp32 row-major K x r (leading dimensions ldx, ldq; X and Q
+ * must not overlap), r a multiple of 256 in [256, 16384], K >= r, K * 256 <= 2^31; Z the K x r dust of
+ * kcholqr.py:83-89 (leading dimension r), block j using its columns j .. j + 255.  Each block is projected against the
+ * finished ones twice (band Gram, W - P (P^T W) on the tensor cores, in place in Q), orthonormalised by the orth
+ * sequence, projected and orthonormalised once more.  Stream-ordered, no host synchronisation, deterministic.  The
+ * workspace (spanqr_workspace_bytes_borth) begins with a status word read by spanqr_read_status.
+ */
+int spanqr_workspace_bytes_borth(int K, int r, size_t* bytes);
+int spanqr_borth_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z, void* ws,
+                     size_t ws_bytes, spanqr_stream_t stream);
 
 /*
  * orth of one shape as one CUDA graph (no reference counterpart; the reference launches kernel by kernel from Python,

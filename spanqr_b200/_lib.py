@@ -26,6 +26,8 @@ SIGNATURES = {
     "spanqr_noalloc_read_status": (_I, [_P, ctypes.POINTER(_I)]),
     "spanqr_workspace_bytes_mixed": (_I, [_P, _I, _I, ctypes.POINTER(_SZ)]),
     "spanqr_orth_mixed_f32": (_I, [_P, _P, _P, _I, _I, _P, _P, _SZ, _P]),
+    "spanqr_workspace_bytes_borth": (_I, [_I, _I, ctypes.POINTER(_SZ)]),
+    "spanqr_borth_f32": (_I, [_P, _LL, _P, _LL, _I, _I, _P, _P, _SZ, _P]),
     "spanqr_orth_graph_create": (_I, [_I, _I, _LL, _LL, _P, _P, _SZ, ctypes.POINTER(_P)]),
     "spanqr_orth_graph_launch": (_I, [_P, _P, _LL, _P, _LL, _P]),
     "spanqr_orth_graph_destroy": (_I, [_P]),

@@ -1,40 +1,31 @@
 """borth: orth for r > 512 (r a multiple of 256), as the reference dispatches it (orth.py:18-19 -> candidates/kbig.py:66-95).
 
-Block Gram-Schmidt with reorthogonalisation (BCGS2) over 256-column blocks: block j (columns j .. j + 255, scaled by
-the power of 2 s of the whole X) has the span of the finished blocks P = Q[:, :j] removed twice,
-W <- W - P (P^T W), and is orthonormalised by the library's orth recipe with its own slice of the full-width dust
-(the K x r draw of the 256-column-wide calls would differ); every later block is then projected and orthonormalised
-once more, so that its dust completions are orthogonal to the earlier blocks too.  Every Cholesky stays 256 wide.
-The projections are plain fp32 GEMMs (torch.mm, cuBLAS), as in the reference; each block's orth runs in
-libspanqr.so through spanqr_orth_f32.
+Block Gram-Schmidt with reorthogonalisation (BCGS2) over 256-column blocks, all of it in libspanqr.so
+(spanqr_borth_f32): block j (columns j .. j + 255, scaled by the power of 2 s of the whole X) has the span of the
+finished blocks P = Q[:, :j] removed twice, W <- W - P (P^T W) (a band Gram and an in-place update on the tensor
+cores), and is orthonormalised by the library's orth recipe with its own slice of the full-width dust (the K x r draw
+of the 256-column-wide calls would differ); every later block is then projected and orthonormalised once more, so that
+its dust completions are orthogonal to the earlier blocks too.  Every Cholesky stays 256 wide.
 """
 import torch
 
-from .core import zdust, workspace, _call
+from . import _lib
+from .core import zdust, _lock
 
 BLOCK = 256
-_ZB = {}
+_WS = {}
 
 
-def _pow2_scale(m):
-    """candidates/kcholqr.py:29-30 on a device scalar: 2^-round(log2 m) for m > 0 (NaN and 0 give 1)"""
-    return torch.where(m > 0, torch.exp2(-torch.round(torch.log2(m.clamp_min(1e-38)))), torch.ones_like(m))
-
-
-def _block_dust(K, r, dev):
-    """the full-width dust Z (K x r, seed 20261018, unit columns) cut into contiguous 256-column blocks"""
-    key = (K, r, str(dev))
-    if key not in _ZB:
-        Z = zdust(K, r, dev)
-        _ZB[key] = [Z[:, j:j + BLOCK].contiguous() for j in range(0, r, BLOCK)]
-    return _ZB[key]
-
-
-def _orth_z(W, Z, stream):
-    K, b = W.shape
-    Q = torch.empty_like(W)
-    _call(W, Q, Z, workspace(W.device, K, b, 1, stream), stream.cuda_stream)
-    return Q
+def _workspace(dev, stream, K, r):
+    key = (str(dev), stream.cuda_stream, K, r)
+    ws = _WS.get(key)
+    if ws is None:
+        n = _lib.ctypes.c_size_t()
+        _lib.check(_lib.lib().spanqr_workspace_bytes_borth(K, r, _lib.ctypes.byref(n)), f"borth({K}x{r})")
+        ws = torch.empty(n.value, dtype=torch.uint8, device=dev)
+        with _lock:
+            ws = _WS.setdefault(key, ws)
+    return ws
 
 
 def borth(X):
@@ -45,18 +36,8 @@ def borth(X):
     dev = X.device
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev)
-        Zs = _block_dust(K, r, dev)
         Q = torch.empty_like(X)
-        s = _pow2_scale(torch.linalg.vector_norm(X, ord=float("inf")))
-        for jb, j in enumerate(range(0, r, BLOCK)):
-            W = X[:, j:j + BLOCK] * s
-            if j:
-                P = Q[:, :j]
-                W = W - P @ (P.T @ W)
-                W = W - P @ (P.T @ W)
-            W = _orth_z(W, Zs[jb], stream)
-            if j:
-                W = W - P @ (P.T @ W)
-                W = _orth_z(W, Zs[jb], stream)
-            Q[:, j:j + BLOCK] = W
+        ws = _workspace(dev, stream, K, r)
+        _lib.check(_lib.lib().spanqr_borth_f32(X.data_ptr(), r, Q.data_ptr(), r, K, r, zdust(K, r, dev).data_ptr(),
+                                               ws.data_ptr(), ws.numel(), stream.cuda_stream), f"borth({K}x{r})")
     return Q

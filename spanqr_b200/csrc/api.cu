@@ -28,9 +28,9 @@ int cuda_fail(cudaError_t e) {
 }
 
 // ---- optional per-kernel timing (spanqr_timing_*) ----
-enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_GRAM_ACC, K_COUNT };
-const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce",
-                                         "k_chol", "k_trsm_w", "k_trsm", "k_ns_update", "k_gram_tc_acc"};
+enum Kind { K_SETUP = 0, K_ABSMAX, K_GRAM, K_REDUCE, K_CHOL, K_TRSM_W, K_TRSM, K_NS, K_GRAM_ACC, K_COPY, K_BAND, K_PROJ, K_COUNT };
+const char* const KIND_NAMES[K_COUNT] = {"k_setup", "k_absmax", "k_gram_tc", "k_gram_reduce", "k_chol", "k_trsm_w", "k_trsm",
+                                         "k_ns_update", "k_gram_tc_acc", "k_scale_copy", "k_band_image", "k_project"};
 struct TimedLaunch {
     int kind;
     cudaEvent_t a, b;
@@ -119,26 +119,29 @@ T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws)
 // The solve on the tensor cores: one panel for n <= 256; for n > 256 the first 8 blocks, the product of those with
 // the W tiles below them (the second panel's start) and the second panel.
 cudaError_t run_trsm(PtrArg p, Src src, int K, int n, long long ldq, int B, const char* maps, const float* Z,
-                     ScaleArg sc, float eps, const char* W, float* scratch, int* status, cudaStream_t st) {
+                     long long ldz, ScaleArg sc, float eps, const char* W, float* scratch, int* status, cudaStream_t st) {
     const int nb = n / TB;
     if (nb <= 8)
         return timed(K_TRSM, st, [&] {
-            return launch_trsm_tc(p, src, K, n, ldq, B, 0, nb, nullptr, maps, Z, sc, eps, W, status, st);
+            return launch_trsm_tc(p, src, K, n, ldq, B, 0, nb, nullptr, maps, Z, ldz, sc, eps, W, status, st);
         });
     cudaError_t e = timed(K_TRSM, st, [&] {
-        return launch_trsm_tc(p, src, K, n, ldq, B, 0, 8, nullptr, maps, Z, sc, eps, W, status, st);
+        return launch_trsm_tc(p, src, K, n, ldq, B, 0, 8, nullptr, maps, Z, ldz, sc, eps, W, status, st);
     });
     if (e == cudaSuccess)
         e = timed(K_TRSM, st, [&] { return launch_trsm_panel_product(p, K, n, ldq, B, 8, nb - 8, maps, W, scratch, status, st); });
     if (e == cudaSuccess)
         e = timed(K_TRSM, st, [&] {
-            return launch_trsm_tc(p, src, K, n, ldq, B, 8, nb - 8, scratch, maps, Z, sc, eps, W, status, st);
+            return launch_trsm_tc(p, src, K, n, ldq, B, 8, nb - 8, scratch, maps, Z, ldz, sc, eps, W, status, st);
         });
     return e;
 }
 
 // The pass sequence of kcholqr_f for B matrices whose pointers are in the workspace table (filled by k_setup_*).
-int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, void* ws, cudaStream_t st) {
+// Z: the dust, K x r with leading dimension ldz (r when 0).
+int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, void* ws, cudaStream_t st,
+             long long ldz = 0) {
+    if (ldz == 0) ldz = r;
     const Layout l = layout(K, r, B);
     const GramPlan gp = gram_tc_plan(K, r);
     PtrArg p{at<MatPtr>(ws, l.ptrs), MatPtr{nullptr, nullptr}};
@@ -174,7 +177,7 @@ int run_orth(int K, int r, int B, long long ldx, long long ldq, const float* Z, 
             return launch_chol(G, Lm, Li, r, B, rowsq, gram_sq_parts(gp), nullptr, scal + (size_t)pass * B, 0, st);
         }));
         SPQ_TRY(timed(K_TRSM_W, st, [&] { return launch_trsm_w(Lm, Li, r, B, W, st); }));
-        SPQ_TRY(run_trsm(p, first ? SRC_X : SRC_Q, K, r, ldq, B, maps, first ? Z : nullptr, sc, first ? EPS : 0.0f, W,
+        SPQ_TRY(run_trsm(p, first ? SRC_X : SRC_Q, K, r, ldq, B, maps, first ? Z : nullptr, ldz, sc, first ? EPS : 0.0f, W,
                          at<float>(ws, l.nss), status, st));
     }
     for (int it = 0; it < NS_STEPS; ++it) {
@@ -476,6 +479,119 @@ int spanqr_orth_graph_destroy(spanqr_graph_t g) {
 
 }  // extern "C"
 
+// ---- block Gram-Schmidt for r > 512 (candidates/kbig.py:66-95, BCGS2 over 256-column blocks) ----
+// Per block j (columns j .. j + 255): W = s X[:, j:j+256] is copied into Q's block (s = pow2_scale(max |X|) of the
+// whole X), has the span of the finished blocks P = Q[:, :j] removed twice (W <- W - P (P^T W): a band Gram, -T as an
+// operand image, the in-place tensor-core update), is orthonormalised in place by the orth sequence at width 256 with
+// the dust's own 256 columns, and, for j > 0, is projected and orthonormalised once more.  The workspace starts with
+// the orth layout of (K, 256, 1), so its status word is the one spanqr_read_status reads; the set-ups of the later
+// blocks' orth sequences keep it.
+namespace {
+struct BorthLayout {
+    size_t maxbits, maps, P, img, total;
+};
+
+BorthLayout borth_layout(int K, int r) {
+    BorthLayout l;
+    size_t o = al256(layout(K, BLOCK_W, 1).total);
+    l.maxbits = o; o += 256;
+    l.maps = o;    o += al256((size_t)TMAPS_PER_MATRIX * 128);
+    size_t pb = 0;
+    for (int j = BLOCK_W; j < r; j += BLOCK_W) {
+        const GramPlan gp = gram_band_plan(K, j);
+        const size_t b = sizeof(float) * (size_t)gp.S * gp.tiles * GRAM_TILE * GRAM_TILE;
+        if (b > pb) pb = b;
+    }
+    l.P = o;       o += al256(pb);
+    l.img = o;     o += al256(r > BLOCK_W ? band_img_bytes(r - BLOCK_W) : 0);
+    l.total = o;
+    return l;
+}
+
+constexpr int BORTH_MAX_R = 16384;
+
+int check_borth_shape(int K, int r) {
+    if (r < BLOCK_W || r > BORTH_MAX_R || r % BLOCK_W || K < r) return SPANQR_ERR_SHAPE;
+    return check_shape(K, BLOCK_W, 1);
+}
+
+// W <- W - P (P^T W) for the block at column j of Q, in place
+int project(float* Q, long long ldq, int K, int j, const char* maps, float* P, char* img, int* status, cudaStream_t st) {
+    const GramPlan gp = gram_band_plan(K, j);
+    const PtrArg q{nullptr, MatPtr{Q, Q}};
+    cudaError_t e = timed(K_GRAM, st, [&] {
+        return launch_gram_tc(q, SRC_Q, K, j + BLOCK_W, ldq, 1, gp, ScaleArg{nullptr, nullptr}, GRAM_PLAIN, P, status, st);
+    });
+    if (e == cudaSuccess) e = timed(K_BAND, st, [&] { return launch_band_image(P, gp, j, img, st); });
+    if (e == cudaSuccess) e = timed(K_PROJ, st, [&] { return launch_project(q, K, j + BLOCK_W, ldq, j, maps, img, status, st); });
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+// the orth sequence at width 256, in place on Q's block at column j, with the dust's columns j .. j + 255
+int block_orth(float* Q, long long ldq, int K, int j, const float* Z, long long ldz, void* ws, cudaStream_t st) {
+    const Layout l = layout(K, BLOCK_W, 1);
+    cudaError_t e = timed(K_SETUP, st, [&] {
+        return launch_setup_strided(at<MatPtr>(ws, l.ptrs), Q + j, 0, Q + j, 0, 1, at<uint32_t>(ws, l.maxbits), nullptr, st);
+    });
+    if (e != cudaSuccess) return cuda_fail(e);
+    return run_orth(K, BLOCK_W, 1, ldq, ldq, Z + j, ws, st, ldz);
+}
+}  // namespace
+
+extern "C" {
+
+int spanqr_workspace_bytes_borth(int K, int r, size_t* bytes) {
+    if (!bytes) return SPANQR_ERR_ARG;
+    const int rc = check_borth_shape(K, r);
+    if (rc) return rc;
+    *bytes = borth_layout(K, r).total;
+    return SPANQR_OK;
+}
+
+int spanqr_borth_f32(const float* X, long long ldx, float* Q, long long ldq, int K, int r, const float* Z, void* ws,
+                     size_t ws_bytes, spanqr_stream_t stream) {
+    int rc = check_borth_shape(K, r);
+    if (rc) return rc;
+    if (!X || !Q || !Z || !a16(X) || !a16(Q) || !a16(Z)) return SPANQR_ERR_ARG;
+    if (ldx < r || ldq < r || ldx % 4 || ldq % 4) return SPANQR_ERR_ARG;
+    {   // Q is written while X is still read: the two must not overlap
+        const uintptr_t x0 = reinterpret_cast<uintptr_t>(X), x1 = x0 + sizeof(float) * ((size_t)(K - 1) * ldx + r);
+        const uintptr_t q0 = reinterpret_cast<uintptr_t>(Q), q1 = q0 + sizeof(float) * ((size_t)(K - 1) * ldq + r);
+        if (x0 < q1 && q0 < x1) return SPANQR_ERR_ARG;
+    }
+    const BorthLayout bl = borth_layout(K, r);
+    if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0 || ws_bytes < bl.total) return SPANQR_ERR_WORKSPACE;
+    const Layout l = layout(K, BLOCK_W, 1);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int* status = at<int>(ws, l.status);
+    uint32_t* maxall = at<uint32_t>(ws, bl.maxbits);
+    char* maps = at<char>(ws, bl.maps);
+    float* P = at<float>(ws, bl.P);
+    char* img = at<char>(ws, bl.img);
+    const PtrArg x{nullptr, MatPtr{X, Q}};
+    cudaError_t e = timed(K_SETUP, st, [&] {
+        return launch_setup_strided(at<MatPtr>(ws, l.ptrs), X, 0, Q, 0, 1, maxall, status, st);
+    });
+    if (e == cudaSuccess) e = timed(K_ABSMAX, st, [&] { return launch_absmax(x, K, r, ldx, 1, maxall, st); });
+    if (e != cudaSuccess) return cuda_fail(e);
+    for (int j = 0; j < r; j += BLOCK_W) {
+        e = timed(K_COPY, st, [&] { return launch_scale_copy(X + j, ldx, Q + j, ldq, K, BLOCK_W, maxall, st); });
+        if (e == cudaSuccess && j > 0)
+            e = timed(K_SETUP, st, [&] { return launch_tmaps(PtrArg{nullptr, MatPtr{Q, Q}}, K, j, ldq, ldq, 1, ws, maps, st); });
+        if (e != cudaSuccess) return cuda_fail(e);
+        for (int t = 0; j > 0 && t < 2; ++t)
+            if ((rc = project(Q, ldq, K, j, maps, P, img, status, st))) return rc;
+        if ((rc = block_orth(Q, ldq, K, j, Z, r, ws, st))) return rc;
+        if (j > 0) {
+            if ((rc = project(Q, ldq, K, j, maps, P, img, status, st))) return rc;
+            if ((rc = block_orth(Q, ldq, K, j, Z, r, ws, st))) return rc;
+        }
+    }
+    return SPANQR_OK;
+}
+
+}  // extern "C"
+
 // ---- orth without any allocation: scratch in a fixed array of the device image ----
 // For callers that may not call cudaMalloc (inside a stream capture that must not add allocations, in a
 // memory-capped sandbox, in a real-time loop).  The array belongs to the library's module: each GPU that loads the
@@ -623,7 +739,7 @@ int spanqr_trsm_f32(const float* X, long long ldx, const float* Z, const float* 
     if (e == cudaSuccess) e = launch_trsm_w(L, Li, n, 1, at<char>(ws, l.W), st);
     if (e == cudaSuccess) e = launch_tmaps(p, K, n, ldx, ldy, 1, ws, at<char>(ws, l.maps), st);
     if (e == cudaSuccess)
-        e = run_trsm(p, SRC_X, K, n, ldy, 1, at<char>(ws, l.maps), Z, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f,
+        e = run_trsm(p, SRC_X, K, n, ldy, 1, at<char>(ws, l.maps), Z, n, ScaleArg{nullptr, d_s}, Z ? eps : 0.0f,
                      at<char>(ws, l.W), at<float>(ws, l.nss), at<int>(ws, l.status), st);
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }

@@ -49,6 +49,20 @@ GramPlan gram_tc_plan(int K, int n) {
     g.tiles = g.nt * (g.nt + 1) / 2;
     g.KS = GRAM_TC_SPLIT;
     g.S = (K + g.KS - 1) / g.KS;
+    g.b0 = 0;
+    return g;
+}
+
+// the band of block Gram-Schmidt: 512-row splits, doubled (up to 2048 rows) while the grid still has four CTAs per SM,
+// so that tall matrices write fewer partials; a function of (K, j) only
+GramPlan gram_band_plan(int K, int j) {
+    GramPlan g;
+    g.b0 = j / TILE;
+    g.nt = g.b0 + BLOCK_W / TILE;
+    g.tiles = g.b0 * (g.nt - g.b0);
+    g.KS = GRAM_TC_SPLIT;
+    while (g.KS < 4 * GRAM_TC_SPLIT && (long long)g.tiles * ((K + 2 * g.KS - 1) / (2 * g.KS)) >= 4 * 148) g.KS *= 2;
+    g.S = (K + g.KS - 1) / g.KS;
     return g;
 }
 
@@ -70,7 +84,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
 
     const int tile = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
     int ti, tj;
-    upper_tile(tile, gp.nt, ti, tj);
+    gram_tile_of(gp, tile, ti, tj);
     const bool diag = ti == tj;
     const MatPtr mp = p.tab ? p.tab[b] : p.one;
     const float* __restrict__ Y = (src == SRC_X) ? mp.X : mp.Q;
@@ -284,7 +298,7 @@ __global__ void __launch_bounds__(PLAIN_NT, 2) k_gram_tc_plain(PtrArg p, Src src
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + PLAIN_BUF + 64);
     const int tile = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
     int ti, tj;
-    upper_tile(tile, gp.nt, ti, tj);
+    gram_tile_of(gp, tile, ti, tj);
     const bool diag = ti == tj;
     const MatPtr mp = p.tab ? p.tab[b] : p.one;
     const float* __restrict__ Y = (src == SRC_X) ? mp.X : mp.Q;

@@ -12,8 +12,11 @@
 // products, so its new values wait in `scratch` and are copied in after the last half.
 // Product mode (MODE 1, for the triangular solve of n > 256): the same pipeline computes only the accumulator
 // sum_{k < j0} Y_k [W_{j0, k}; ...; W_{j0+nbp-1, k}]^T from the solve's W image (A = the first 32 j0 columns of Q,
-// B = the stacked W tiles of block column k) and writes it to `scratch` (K x 256 per matrix).  Accuracy: |Q D| is about 1e-2 |Q| or less, so 3xTF32 and the
-// truncating fp32 accumulation leave errors below one ulp of Q.
+// B = the stacked W tiles of block column k) and writes it to `scratch` (K x 256 per matrix).
+// Projection mode (MODE 2, block Gram-Schmidt for r > 512, candidates/kbig.py:66-95 W - P (P^T W)): A = the first j0
+// columns of Q (the finished blocks P), B = -T (T = P^T W, k_band_image), N = 256; the result is added to the block
+// W = Q[:, j0 .. j0 + 256) in place.  Accuracy: |Q D| is about 1e-2 |Q| or less, so 3xTF32 and the truncating fp32
+// accumulation leave errors below one ulp of Q.
 #include "kernels.h"
 #include "tc.cuh"
 
@@ -55,7 +58,8 @@ __global__ void k_d_image(const float* __restrict__ D_all, int n, char* __restri
     tc::store2_at(part, part + (size_t)N * 128, tc::swz_off(rr, q), v);
 }
 
-template <int NH, int MODE>   // NH: column halves (1 for n <= 256, 2 above); MODE: 0 update, 1 solve panel product
+template <int NH, int MODE>   // NH: column halves (1 for n <= 256, 2 above); MODE: 0 update, 1 solve panel product,
+                              // 2 projection
 __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long long ldq, const char* __restrict__ maps,
                                                  const char* __restrict__ img_all, float* __restrict__ scratch,
                                                  int* __restrict__ status, int ncontr, int Nout, int j0) {
@@ -73,6 +77,7 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
     const int nchunks = ncontr / CH;              // chunks of the contraction
     constexpr int nh = NH;
     const int N = Nout;                           // width of a column half (MODE 1: of the panel product)
+    const int oc0 = MODE == 2 ? j0 : 0;           // the output's first column
     const int total = nh * nchunks;               // chunks over all halves: g = h * nchunks + c
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -96,14 +101,14 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
         const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
         // the addend y (this row of Q before the update; nothing writes it before the last half's epilogue) is loaded
         // one 32-column block ahead: the first before the products are done, each next one during the current one
-        const bool addend = MODE == 0 && row < K;
+        const bool addend = MODE != 1 && row < K;
         float4 yv[8], yn[8];
         auto load_y = [&](float4 (&y)[8], int col) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) y[i] = addend ? *reinterpret_cast<const float4*>(qr + col + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
         };
         for (int h = 0; h < nh; ++h) {
-            const int c0 = h * N;
+            const int c0 = oc0 + h * N;
             load_y(yv, c0);
             const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], (uint32_t)(h & 1), 500);
             if (!__all_sync(0xffffffffu, done && !*err)) {   // per warp: tcgen05.ld needs the whole warp
@@ -212,7 +217,9 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
         // ---------------- copies ----------------
         if (lane == 0) {
             const void* map = maps + ((size_t)b * TMAPS_PER_MATRIX + TMAP_Q) * 128;
-            const char* img = img_all + (size_t)b * (MODE == 0 ? ns_dimg_bytes(n) : wcol_off(n / CH, n / CH));
+            const char* img = img_all + (size_t)b * (MODE == 0   ? ns_dimg_bytes(n)
+                                                     : MODE == 1 ? wcol_off(n / CH, n / CH)
+                                                                 : band_img_bytes(ncontr));
             const uint32_t pbytes = (uint32_t)(N * 128);   // one half's rows of one part (hi or lo) of a D chunk
             tc::tmap_acquire(map);
             int n_raw[2] = {0, 0}, n_d[2] = {0, 0};
@@ -232,6 +239,8 @@ __global__ void __launch_bounds__(NT, 1) k_ns_ws(PtrArg p, int K, int n, long lo
                 if (MODE == 0) {
                     const char* chunk = img + (size_t)c * 2 * n * 128 + (size_t)h * 2 * pbytes;   // hi rows, lo rows
                     tc::bulk_g2s(DB + st * 2 * DPART, chunk, 2 * pbytes, &bars[B_D + st]);
+                } else if (MODE == 2) {   // chunk c of -T: hi rows, lo rows
+                    tc::bulk_g2s(DB + st * 2 * DPART, img + (size_t)c * 2 * pbytes, 2 * pbytes, &bars[B_D + st]);
                 } else {
                     // block column c of the W image: tiles j0 .. of its trailing list (hi), and the same in the lo list
                     const int NB = n / CH;
@@ -281,6 +290,12 @@ cudaError_t launch_trsm_panel_product(PtrArg p, int K, int n, long long ldq, int
                                       const char* W, float* scratch, int* status, cudaStream_t st) {
     if (n > 512 || n % CH || j0 < 1 || nbp < 1 || nbp > 8 || (j0 + nbp) * CH > n || !scratch) return cudaErrorInvalidValue;
     return launch_k<1, 1>(p, K, n, ldq, B, maps, W, scratch, status, j0 * CH, nbp * CH, j0, st);
+}
+
+cudaError_t launch_project(PtrArg p, int K, int n, long long ldq, int j, const char* maps, const char* img,
+                           int* status, cudaStream_t st) {
+    if (j < BLOCK_W || j % BLOCK_W || j + BLOCK_W > n || ldq < n) return cudaErrorInvalidValue;
+    return launch_k<1, 2>(p, K, n, ldq, 1, maps, img, nullptr, status, j, BLOCK_W, j, st);
 }
 
 }  // namespace spq

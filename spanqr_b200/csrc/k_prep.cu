@@ -11,7 +11,7 @@ __global__ void k_setup_strided(MatPtr* tab, const float* X, long long sX, float
         tab[b].Q = Q + (long long)b * sQ;
         maxbits[b] = 0u;
     }
-    if (b == 0) status[0] = 0;
+    if (b == 0 && status) status[0] = 0;   // null: keep the status of the calls before (block Gram-Schmidt)
 }
 
 __global__ void k_setup_array(MatPtr* tab, const float* const* dX, float* const* dQ, int B, uint32_t* maxbits,

@@ -312,13 +312,13 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
 size_t trsm_w_bytes(int n) { return wcol_off(n / BLK, n / BLK); }
 
 cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, int j0, int nbp, const float* init,
-                           const char* maps, const float* Z, ScaleArg sc, float eps, const char* W, int* status,
-                           cudaStream_t st) {
+                           const char* maps, const float* Z, long long ldz, ScaleArg sc, float eps, const char* W,
+                           int* status, cudaStream_t st) {
     if (n > 512 || n % BLK || nbp < 1 || nbp > MAXNB || j0 < 0 || (j0 + nbp) * BLK > n) return cudaErrorInvalidValue;
     alignas(64) CUtensorMap zmap;
     memset(&zmap, 0, sizeof(zmap));
     if (Z) {
-        cudaError_t e = encode_rows(&zmap, Z, K, n, n, TMAP_BOX_COLS, TMAP_BOX_ROWS);
+        cudaError_t e = encode_rows(&zmap, Z, K, n, ldz, TMAP_BOX_COLS, TMAP_BOX_ROWS);
         if (e != cudaSuccess) return e;
     }
     cudaError_t e = cudaFuncSetAttribute(k_trsm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);

@@ -39,17 +39,20 @@ __global__ void __launch_bounds__(256) k_trsm_w(const float* __restrict__ L_all,
     // thread: row r, columns 4 q .. 4 q + 3 (q = 0..7)
     const int r = threadIdx.x >> 3, q = threadIdx.x & 7;
     float w[4];
+    if (k == j) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = 4 * q + i;
-        if (k == j) {
-            w[i] = (float)sLi[r][c];
-        } else {
-            double acc = 0.0;
+        for (int i = 0; i < 4; ++i) w[i] = (float)sLi[r][4 * q + i];
+    } else {
+        // four chains, each over m in order; sLi[r][m] is loaded once for all four
+        double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll 8
-            for (int m = 0; m < TB; ++m) acc = __fma_rn(sLi[r][m], sL[m][c], acc);
-            w[i] = -__double2float_rn(acc);
+        for (int m = 0; m < TB; ++m) {
+            const double a = sLi[r][m];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = __fma_rn(a, sL[m][4 * q + i], acc[i]);
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = -__double2float_rn(acc[i]);
     }
     tc::store2_at(hi, lo, tc::swz_off(r, q), make_float4(w[0], w[1], w[2], w[3]));
 }

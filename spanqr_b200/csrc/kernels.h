@@ -23,13 +23,26 @@ struct ScaleArg {
     const float* s;           // [B] or null
 };
 
-// Split-K plan of the Gram: 128 x 128 tiles of the upper triangle, splits of a fixed number of rows.
+// Split-K plan of the Gram: 128 x 128 tiles of the upper triangle (or, with b0 > 0, of the band ti < b0 <= tj: the
+// cross product of the first 128 b0 columns with the rest), splits of a fixed number of rows.
 struct GramPlan {
     int nt;      // tiles per side, n / 128 rounded up
-    int tiles;   // upper tiles nt (nt + 1) / 2
+    int tiles;   // upper tiles nt (nt + 1) / 2, or b0 (nt - b0) in band mode
     int S;       // splits
     int KS;      // rows per split
+    int b0;      // 0: the upper triangle; else the first tile column of the band
 };
+
+// tile t of a plan -> (ti, tj)
+__device__ __forceinline__ void gram_tile_of(const GramPlan& gp, int t, int& ti, int& tj) {
+    if (gp.b0 > 0) {
+        const int w = gp.nt - gp.b0;
+        ti = t / w;
+        tj = gp.b0 + t % w;
+    } else {
+        upper_tile(t, gp.nt, ti, tj);
+    }
+}
 
 // the set-up kernel of the strided entry points, k_setup_strided(tab, X, sX, Q, sQ, B, maxbits, status): the only
 // kernel of an orth call that takes X and Q as arguments (every later one reads them from the table)
@@ -100,8 +113,8 @@ cudaError_t launch_trsm_w(const float* L, const float* Li, int n, int B, char* W
 // n <= 512 matrix; input rows by the TMA maps (launch_tmaps), output to Q; `init` (K x 256 floats per matrix, or
 // null) starts the panel's large accumulators; a bounded wait that runs out ORs 0x40 into *status
 cudaError_t launch_trsm_tc(PtrArg p, Src src, int K, int n, long long ldq, int B, int j0, int nbp, const float* init,
-                           const char* maps, const float* Z, ScaleArg sc, float eps, const char* W, int* status,
-                           cudaStream_t st);
+                           const char* maps, const float* Z, long long ldz, ScaleArg sc, float eps, const char* W,
+                           int* status, cudaStream_t st);
 // scratch[b][row][0 .. 32 nbp) = sum_{k < j0} Y_k W_{j0.., k}^T (Y = the first 32 j0 columns of Q): the second
 // panel's start for launch_trsm_tc; a bounded wait that runs out ORs 0x20 into *status
 cudaError_t launch_trsm_panel_product(PtrArg p, int K, int n, long long ldq, int B, int j0, int nbp, const char* maps,
@@ -113,6 +126,22 @@ cudaError_t launch_trsm_panel_product(PtrArg p, int K, int n, long long ldq, int
 __host__ __device__ inline size_t ns_dimg_bytes(int n) { return (size_t)8 * n * n; }
 cudaError_t launch_ns_ws(PtrArg p, int K, int n, long long ldq, int B, const float* D, const char* maps, char* img,
                          float* scratch, int* status, cudaStream_t st);
+
+// ---- block Gram-Schmidt (r > 512, 256-column blocks) ----
+constexpr int BLOCK_W = 256;
+// the band plan for T = P^T W with P = the first j columns and W the next 256 of a K-row matrix (splits of 2048 rows)
+GramPlan gram_band_plan(int K, int j);
+// -T as the update's operand image (B operand rows = W's 256 columns, contraction over P's j columns), from the band
+// partials summed in split order (float-float): j x 256 x 8 bytes per matrix
+__host__ __device__ inline size_t band_img_bytes(int j) { return (size_t)8 * j * BLOCK_W; }
+cudaError_t launch_band_image(const float* P, const GramPlan& gp, int j, char* img, cudaStream_t st);
+// Q[:, j .. j + 256) += Q[:, 0 .. j) (-T), in place, from that image (maps from launch_tmaps over Q); a bounded wait
+// that runs out ORs 0x20 into *status
+cudaError_t launch_project(PtrArg p, int K, int n, long long ldq, int j, const char* maps, const char* img,
+                           int* status, cudaStream_t st);
+// Q[:, 0 .. w) = s X[:, 0 .. w) with s = pow2_scale(max |X|) from *maxbits
+cudaError_t launch_scale_copy(const float* X, long long ldx, float* Q, long long ldq, int K, int w,
+                              const uint32_t* maxbits, cudaStream_t st);
 
 
 

@@ -91,6 +91,32 @@ def test_argument_checks_before_any_device_work():
     assert L.spanqr_selftest_timeout(al, 256, 3 * 10 ** 9, 0, None) == ARG                  # above 2 s
 
 
+@pytest.mark.parametrize("K,r,rc", [(2048, 768, OK), (5120, 1024, OK), (1024, 256, OK), (2048, 640, SHAPE),
+                                    (700, 768, SHAPE), (2048, 16640, SHAPE), (1 << 24, 768, SHAPE)])
+def test_borth_workspace_bytes(K, r, rc):
+    n = ctypes.c_size_t(0)
+    assert _lib.lib().spanqr_workspace_bytes_borth(K, r, ctypes.byref(n)) == rc
+    if rc == OK:
+        assert n.value >= _lib.workspace_bytes(K, 256, 1) + 8 * 256 * (r - 256)
+
+
+def test_borth_argument_checks_before_any_device_work():
+    L = _lib.lib()
+    n = ctypes.c_size_t(0)
+    assert L.spanqr_workspace_bytes_borth(2048, 768, ctypes.byref(n)) == OK
+    need = n.value
+    al = (1 << 20) * 256
+    far = al + (1 << 34)          # a Q that does not overlap X
+    assert L.spanqr_borth_f32(al, 768, far, 768, 2048, 640, al, al, need, None) == SHAPE
+    assert L.spanqr_borth_f32(None, 768, far, 768, 2048, 768, al, al, need, None) == ARG
+    assert L.spanqr_borth_f32(al, 768, far, 768, 2048, 768, None, al, need, None) == ARG     # no dust
+    assert L.spanqr_borth_f32(al + 4, 768, far, 768, 2048, 768, al, al, need, None) == ARG   # misaligned X
+    assert L.spanqr_borth_f32(al, 700, far, 768, 2048, 768, al, al, need, None) == ARG       # ldx < r
+    assert L.spanqr_borth_f32(al, 768, al + 4096, 768, 2048, 768, al, al, need, None) == ARG  # Q overlaps X
+    assert L.spanqr_borth_f32(al, 768, far, 768, 2048, 768, al, al, need - 1, None) == WS    # workspace too small
+    assert L.spanqr_borth_f32(al, 768, far, 768, 2048, 768, al, al + 16, need, None) == WS   # workspace misaligned
+
+
 def test_error_type_names_the_code():
     with pytest.raises(_lib.SpanqrError, match="unsupported shape"):
         _lib.check(SHAPE, "orth")

@@ -353,8 +353,6 @@ __global__ void __launch_bounds__(NT, 1) k_chol_dsm(float* __restrict__ A_all, f
 size_t chol_smem_bytes(int n, int C) { return smem_floats(n / TB, C) * sizeof(float); }
 
 namespace {
-int g_nsm[64] = {};
-
 template <int C>
 cudaError_t launch_c(float* A, float* L, float* Li, int n, int B, const double* rowsq, int nsq, const float* tau_ptr,
                      PassScal* scal, int zero_upper, cudaStream_t st) {
@@ -395,16 +393,9 @@ int chol_cluster_size(int n, int B, int nsm) {
 cudaError_t launch_chol(float* A, float* L, float* Li, int n, int B, const double* rowsq, int nsq,
                         const float* tau_ptr, PassScal* scal, int zero_upper, cudaStream_t st) {
     if (n % TB || n < TB || n > MAX_R) return cudaErrorInvalidValue;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    int nsm = 0;
+    const cudaError_t e = sm_count(&nsm);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64 && g_nsm[dev] == 0) {
-        int v = 0;
-        e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-        g_nsm[dev] = v;
-    }
-    const int nsm = (dev >= 0 && dev < 64) ? g_nsm[dev] : 148;
     switch (chol_cluster_size(n, B, nsm)) {
         case 1: return launch_c<1>(A, L, Li, n, B, rowsq, nsq, tau_ptr, scal, zero_upper, st);
         case 2: return launch_c<2>(A, L, Li, n, B, rowsq, nsq, tau_ptr, scal, zero_upper, st);

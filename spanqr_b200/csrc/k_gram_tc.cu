@@ -249,11 +249,14 @@ __global__ void __launch_bounds__(NT, 1) k_gram_tc(PtrArg p, Src src, int K, int
         const int row = (warp & 3) * 32 + lane;
         float* ptile = P + ((size_t)(b * gp.S + sp) * gp.tiles + tile) * TILE * TILE;
         float* out = ptile + (size_t)row * TILE + (warp >> 2) * 64;
+        // partial rows: 512 bytes apart, 256-byte aligned base
 #pragma unroll
-        for (int i = 0; i < 64; i += 4)
-            *reinterpret_cast<float4*>(out + i) =
-                make_float4(__double2float_rn(acc[i]), __double2float_rn(acc[i + 1]), __double2float_rn(acc[i + 2]),
-                            __double2float_rn(acc[i + 3]));
+        for (int h = 0; h < 64; h += 32) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __double2float_rn(acc[h + i]);
+            tc::st_row32(out + h, v, true);
+        }
         if (diag) {
             // fixed-order sum of the 8 warps' partial sums of squares of each column (warp order 0..7); overwrite the
             // diagonal of the partial tile

@@ -116,9 +116,7 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                     for (int i = 0; i < 32; ++i)
                         if (c0 + i == a) big[i] = __double2float_rn(d);
                 }
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4*>(row + i) = make_float4(big[i], big[i + 1], big[i + 2], big[i + 3]);
+                tc::st_row32(row, big, true);   // partial rows: 512 bytes apart, 256-byte aligned base
             }
         }
     } else if (warp < 8) {

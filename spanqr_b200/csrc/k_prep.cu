@@ -1,7 +1,28 @@
 // Call set-up (pointer tables, zeroed accumulators) and max |X| per matrix.
+#include <atomic>
+
 #include "kernels.h"
 
 namespace spq {
+
+namespace {
+std::atomic<int> g_nsm[64];
+}
+
+cudaError_t sm_count(int* nsm) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaDeviceGetAttribute(nsm, cudaDevAttrMultiProcessorCount, dev);
+    int v = g_nsm[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+        e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        g_nsm[dev].store(v, std::memory_order_relaxed);
+    }
+    *nsm = v;
+    return cudaSuccess;
+}
 
 __global__ void k_setup_strided(MatPtr* tab, const float* X, long long sX, float* Q, long long sQ, int B,
                                 uint32_t* maxbits, int* status) {

@@ -104,10 +104,11 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
                 const int row = row0 + warp * 32 + lane;
                 float v[32];
                 const float* ir = init + ((size_t)b * K + (row < K ? row : 0)) * 256 + c;
+                if (row < K) {
+                    tc::ld_row32(ir, v, true);   // workspace rows: 1 KB apart, 256-byte aligned base
+                } else {
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 x = row < K ? *reinterpret_cast<const float4*>(ir + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    v[i] = x.x; v[i + 1] = x.y; v[i + 2] = x.z; v[i + 3] = x.w;
+                    for (int i = 0; i < 32; ++i) v[i] = 0.f;
                 }
                 tc::tmem_st32(tlane + (uint32_t)c, v);
             } else {
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
         tc::bar_sync(2, 128 + 32);   // with the issue warp: accumulators zeroed before the first product
         const int me = warp * 32 + lane, rowe = row0 + me;
         float* qrow = (p.tab ? p.tab[b] : p.one).Q + (long long)rowe * ldq;
+        const bool w8 = tc::al32(qrow);   // 32-byte stores where the row allows them
         // exits are decided per warp (__all_sync): tcgen05.ld needs the whole warp
         for (int j = 0; j < nb; ++j) {
             if (!__all_sync(0xffffffffu, !*err && tc::mbar_wait(&bars[B_ACC], (uint32_t)(j & 1)))) {   // acc[j] done
@@ -141,12 +143,7 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
                 tc::fence_async_smem();
                 tc::mbar_arrive(&bars[B_Y]);
             }
-            if (rowe < K) {
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    *reinterpret_cast<float4*>(qrow + 32 * (j0 + j) + 4 * q) =
-                        make_float4(big[4 * q], big[4 * q + 1], big[4 * q + 2], big[4 * q + 3]);
-            }
+            if (rowe < K) tc::st_row32(qrow + 32 * (j0 + j), big, w8);
         }
     } else if (warp < 8) {
         // ---------------- convert warps: raw A_c -> s x + eps z -> tf32 hi | lo, in place ----------------

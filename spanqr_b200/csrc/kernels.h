@@ -71,6 +71,8 @@ constexpr int TMAP_BOX_COLS = 32;
 constexpr int TMAP_BOX_ROWS = 128;
 constexpr int GRAM_BOX_COLS = 128;
 constexpr int GRAM_BOX_ROWS = 32;
+// streaming multiprocessors of the current device (looked up once per device)
+cudaError_t sm_count(int* nsm);
 cudaError_t encode_rows(CUtensorMap* m, const void* base, int rows, int cols, long long ld, int box_cols, int box_rows);
 cudaError_t launch_tmaps(PtrArg p, int K, int r, long long ldx, long long ldq, int B, const void* any, char* maps,
                          cudaStream_t st);

@@ -341,3 +341,48 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 }
 }  // namespace tc
 }  // namespace spq
+
+namespace spq {
+namespace tc {
+// 32-byte global accesses (sm_100): eight consecutive floats at a 32-byte aligned address.  A warp whose threads each
+// own one row moves 32 full sectors per instruction instead of 32 half sectors with 16-byte accesses.
+__device__ __forceinline__ void ld8(const float* p, float* v) {
+    asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+                 : "l"(p));
+}
+__device__ __forceinline__ void st8(float* p, const float* v) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
+                 "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                 : "memory");
+}
+}  // namespace tc
+}  // namespace spq
+
+namespace spq {
+namespace tc {
+// 32 consecutive floats of one row to / from global memory: 32-byte accesses when `w8` (p 32-byte aligned), else 16
+__device__ __forceinline__ void st_row32(float* p, const float* v, bool w8) {
+    if (w8) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 8) st8(p + k, v + k);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) *reinterpret_cast<float4*>(p + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+    }
+}
+__device__ __forceinline__ void ld_row32(const float* p, float* v, bool w8) {
+    if (w8) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 8) ld8(p + k, v + k);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 32; k += 4) {
+            const float4 t = *reinterpret_cast<const float4*>(p + k);
+            v[k] = t.x, v[k + 1] = t.y, v[k + 2] = t.z, v[k + 3] = t.w;
+        }
+    }
+}
+__device__ __forceinline__ bool al32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31) == 0; }
+}  // namespace tc
+}  // namespace spq

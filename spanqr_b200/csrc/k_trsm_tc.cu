@@ -220,12 +220,9 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
                 tc::fence_after_sync();
                 const int t = nb - 1 - j;   // trailing tiles of column j in this panel: blocks j + 1 .. nb - 1
                 const uint32_t yj = tc::smem_u32(AB + (j % NSLOT) * SLOT), wt = tc::smem_u32(WT + (j & 1) * WTBUF);
-                // T1: block j + 1, which is then complete
-                products(32 * (j + 1), yj, yj + YT, wt, wt + (uint32_t)t * WPART, BLK);
+                // blocks j + 1 .. nb - 1 in one product (block j + 1 is then complete)
+                products(32 * (j + 1), yj, yj + YT, wt, wt + (uint32_t)t * WPART, BLK * t);
                 tc::mma_commit(&bars[B_ACC]);
-                // T2: the later blocks, one product
-                if (t > 1)
-                    products(32 * (j + 2), yj, yj + YT, wt + WPART, wt + (uint32_t)(t + 1) * WPART, BLK * (t - 1));
                 tc::mma_commit(&bars[B_FREE + j % NSLOT]);
             }
             if (!ok) {

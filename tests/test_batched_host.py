@@ -7,6 +7,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from spanqr_b200 import batched
 from spanqr_b200.batched import partition, layout, exchange, wave_of, wave_layout
 
 
@@ -16,6 +17,19 @@ def test_partition_equal_costs_is_contiguous_and_balanced():
         assert o == sorted(o)
         counts = [o.count(q) for q in range(W)]
         assert max(counts) - min(counts) <= 1 and sum(counts) == B
+
+
+@pytest.mark.parametrize("n,chunks", [(96, 16), (96, 12), (40, 12), (13, 4), (8, 12), (96, 1), (5, 3)])
+def test_host_parts_tile_the_batch_in_order(n, chunks):
+    """the host path's chunks: consecutive, in index order, none above ceil(n / chunks); with the ramp the first two
+    and last two are smaller than the middle ones"""
+    idx = list(range(100, 100 + n))
+    parts, step = batched._host_parts(idx, chunks)
+    assert [i for p in parts for i in p] == idx
+    assert step == -(-n // max(1, min(chunks, n))) and all(0 < len(p) <= step for p in parts)
+    sizes = [len(p) for p in parts]
+    if batched.HOST_RAMP and step >= 4 and len(parts) > 4:
+        assert sizes[0] < sizes[1] < sizes[2] and sizes[-1] < sizes[-2] < sizes[-3]
 
 
 def test_partition_mixed_batch_balances_cost_exactly():

@@ -377,14 +377,14 @@ cudaError_t launch_c(float* A, float* L, float* Li, int n, int B, const double* 
 }
 }  // namespace
 
-// CTAs per matrix: 8 above r 256 (the tiles need the shared memory of 8 SMs).  Up to r 256 a batch of 8 or more
-// matrices runs one CTA per matrix (the most work per SM; batches are often split over concurrent streams, so the
-// SMs are busy anyway), and a smaller batch spreads each matrix over up to 8 SMs (at most one per block row, the whole
-// batch within half of the SMs) for latency.
+// CTAs per matrix: 8 above r 256 (the tiles need the shared memory of 8 SMs).  Up to r 256 each matrix spreads over
+// up to 8 SMs (at most one per block row) while the whole batch stays within half of the SMs: a lone matrix or a
+// small batch (a rank's share of a multi-GPU batch) runs at the cluster's latency, a large batch one CTA per matrix
+// (the most work per SM; its parts run on concurrent streams, so the SMs are busy anyway).  The bits do not depend on
+// the cluster size.
 int chol_cluster_size(int n, int B, int nsm) {
     const int nb = n / TB;
     if (nb > 8) return 8;
-    if (B >= 8) return 1;
     int C = 1;
     while (C < 8 && 2 * C <= nb && (long long)B * 2 * C <= nsm / 2) C *= 2;
     return C;

@@ -194,18 +194,29 @@ def _check_host(X, name):
 
 HOST_SLOTS = 4        # device buffers in flight in the host path
 HOST_COMPUTE = 2      # compute streams in the host path (consecutive chunks' kernels overlap)
-HOST_RAMP = True      # smaller first and last chunks
+HOST_RAMP = True      # smaller first and last chunks (batches cut into at least HOST_RAMP_MIN chunks)
+HOST_RAMP_MIN = 12
+HOST_PER_CHUNK = 6    # default chunking: about this many matrices per chunk, 4 to HOST_CHUNKS chunks
+
+
+def _default_chunks(n):
+    """chunks for n host matrices: every chunk's orth costs a kernel-chain latency (~0.5 ms) on top of its share of
+    the work, so small batches (a rank's share of a multi-GPU batch) use few chunks of several matrices and large ones
+    HOST_CHUNKS (config-3 shares on one B200: 12 matrices 3.8 -> 1.9 ms as 4 chunks instead of 12, 24 matrices 4.2 ->
+    3.1 ms)"""
+    return max(1, min(n, HOST_CHUNKS, max(4, n // HOST_PER_CHUNK)))
 
 
 def _host_parts(idx, chunks):
-    """idx cut into consecutive parts of at most ceil(len / chunks) items; with HOST_RAMP the first two parts hold a
-    quarter and a half of that and so do the last two, so that the first kernels start, and the last copies out end,
-    sooner (the link is idle in one direction until the first chunk is computed, and in the other after the last
-    chunk is copied in)"""
+    """idx cut into consecutive parts of at most ceil(len / chunks) items; with HOST_RAMP (at least HOST_RAMP_MIN
+    chunks) the first two parts hold a quarter and a half of that and so do the last two, so that the first kernels
+    start, and the last copies out end, sooner (the link is idle in one direction until the first chunk is computed,
+    and in the other after the last chunk is copied in)"""
     n = len(idx)
-    step = -(-n // max(1, min(chunks, n)))
+    nch = max(1, min(chunks, n))
+    step = -(-n // nch)
     sizes = None
-    if HOST_RAMP and step >= 4:
+    if HOST_RAMP and nch >= HOST_RAMP_MIN and step >= 4:
         head = [step // 4, step // 2]
         rest = n - 2 * sum(head)
         if rest >= step:
@@ -275,11 +286,12 @@ def _run_host(Xs, Qs, device, chunks):
 HOST_CHUNKS = 16      # pieces of a host batch: config 3 on one B200, 10.3k matrices/s at 16 with the ramp (10.2k at 12)
 
 
-def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=HOST_CHUNKS):
+def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=None):
     """Q_i = orth(X_i) for every matrix.  Xs: a list of fp32 CUDA [K_i, r_i] tensors on one device, or one
     [B, K, r] tensor.  Returns a list of Qs (a [B, K, r] tensor for a tensor input).  Under torch.distributed the
     work is split across the ranks of `group` (default: the world) and the results all-gathered (gather=True).
-    A list of CPU tensors runs on the current CUDA device with the copies overlapped (`chunks` pieces) and returns CPU
+    A list of CPU tensors runs on the current CUDA device with the copies overlapped (`chunks` pieces; by default about
+    HOST_PER_CHUNK matrices per piece, 4 to HOST_CHUNKS pieces) and returns CPU
     tensors (`out`, if given); under torch.distributed that needs gather=False."""
     if not torch.is_tensor(Xs) and len(Xs) and torch.is_tensor(Xs[0]) and not Xs[0].is_cuda:
         Xs = list(Xs)
@@ -295,7 +307,8 @@ def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=HOST_CHUNKS):
             out = [torch.empty(x.shape, dtype=torch.float32, pin_memory=True) if owner[i] == rank else None
                    for i, x in enumerate(Xs)]
         mine = [i for i in range(len(Xs)) if owner[i] == rank]
-        _run_host([Xs[i].contiguous() for i in mine], [out[i] for i in mine], torch.cuda.current_device(), chunks)
+        _run_host([Xs[i].contiguous() for i in mine], [out[i] for i in mine], torch.cuda.current_device(),
+                  _default_chunks(len(mine)) if chunks is None else chunks)
         return [out[i] if owner[i] == rank else None for i in range(len(Xs))]
     stacked = torch.is_tensor(Xs)
     if stacked:

@@ -28,8 +28,17 @@ def test_host_parts_tile_the_batch_in_order(n, chunks):
     assert [i for p in parts for i in p] == idx
     assert step == -(-n // max(1, min(chunks, n))) and all(0 < len(p) <= step for p in parts)
     sizes = [len(p) for p in parts]
-    if batched.HOST_RAMP and step >= 4 and len(parts) > 4:
+    if batched.HOST_RAMP and min(chunks, n) >= batched.HOST_RAMP_MIN and step >= 4 and len(parts) > 4:
         assert sizes[0] < sizes[1] < sizes[2] and sizes[-1] < sizes[-2] < sizes[-3]
+    elif min(chunks, n) < batched.HOST_RAMP_MIN:
+        assert len(parts) == -(-n // step)   # no ramp: equal parts
+
+
+def test_default_host_chunks():
+    """few chunks of several matrices for a small batch (each chunk costs a kernel-chain latency), HOST_CHUNKS for a
+    large one, never more chunks than matrices"""
+    d = batched._default_chunks
+    assert [d(n) for n in (1, 3, 12, 24, 48, 96, 500)] == [1, 3, 4, 4, 8, 16, 16]
 
 
 def test_partition_mixed_batch_balances_cost_exactly():

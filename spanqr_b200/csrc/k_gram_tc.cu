@@ -15,8 +15,9 @@
 // partial.  k_gram_reduce
 // (k_gram.cu) sums the partials in split order.  Which mode runs where: the orth
 // sequence uses the drained mode for its last polish Gram (the reference's compensated gram_split, kcholqr.py:20) and
-// the plain mode for the Grams of r > 256 (k_gram_ws covers r <= 256); the accurate mode serves the component entry
-// point spanqr_gram_f32, the counterpart of the reference's compensated gram_f / gram_split (tri.py:285-375).
+// the plain mode for the Grams of r > 256 (k_gram_ws covers r <= 256) and, with a band plan (tiles ti < b0 <= tj), for
+// T = P^T W of block Gram-Schmidt (r > 512); the accurate mode serves the component entry point spanqr_gram_f32, the
+// counterpart of the reference's compensated gram_f / gram_split (tri.py:285-375).
 // Determinism: the split size (512 rows) and every order depend only on (K, n), never on the batch or the GPU.
 // Compensation: the reference (candidates/tri.py:255-375) Kahan-sums fp32 32-row dots inside a split and adds the
 // splits in fp64; here each group of rows (32 in the accurate mode, 128 in the drained mode) sums its products in the

@@ -64,3 +64,32 @@ def test_borth_rejects_what_the_block_path_cannot_take():
         orth(torch.zeros(700, 768, device="cuda"))    # K < r
     with pytest.raises(ValueError):
         orth(torch.zeros(700, 640, device="cuda"))    # r 640 is padded to 768 > K
+
+
+def test_borth_c_abi_leading_dimensions_and_status():
+    """spanqr_borth_f32 through the C ABI with X a column slice of a wider matrix (ldx > r) and Q written into a wider
+    buffer (ldq > r): the same bits as the contiguous call, the columns outside Q's slice untouched, and the
+    workspace's status word 0 afterwards"""
+    import ctypes
+    from spanqr_b200 import _lib
+    L = _lib.lib()
+    K, r = 2048, 768
+    X = torch.from_numpy(_mixed(K, r, 1e3, 21).astype(np.float32)).cuda()
+    want = orth(X)
+    wide = torch.randn(K, r + 256, device="cuda")
+    wide[:, 128:128 + r] = X
+    Xs = wide[:, 128:128 + r]
+    Qw = torch.full((K, r + 64), 7.0, device="cuda")
+    n = ctypes.c_size_t()
+    assert L.spanqr_workspace_bytes_borth(K, r, ctypes.byref(n)) == 0
+    ws = torch.empty(n.value, dtype=torch.uint8, device="cuda")
+    Z = zdust(K, r, "cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        rc = L.spanqr_borth_f32(Xs.data_ptr(), r + 256, Qw.data_ptr(), r + 64, K, r, Z.data_ptr(), ws.data_ptr(),
+                                n.value, st)
+        assert rc == 0, _lib.lib().spanqr_strerror(rc)
+        status = ctypes.c_int(-1)
+        assert L.spanqr_read_status(ws.data_ptr(), st, ctypes.byref(status)) == 0 and status.value == 0
+        assert torch.equal(Qw[:, :r].contiguous().view(torch.int32), want.view(torch.int32))
+        assert torch.all(Qw[:, r:] == 7.0)

@@ -15,8 +15,9 @@
 // rings run on from item to item, so the next item's copies and conversions proceed during an item's epilogue, and
 // the products resume as soon as the epilogue has read the accumulators out of TMEM.  Each item's arithmetic is the
 // same whichever CTA computes it.
-// Warp roles: 0-3 epilogue (TMEM lanes = the panel's columns), 4-7 convert (raw chunk -> s y -> tf32 hi | lo, float-float
-// squares of the panel's columns), 8 products (one thread), 9 copies (one thread, TMA through the per-matrix maps).
+// Warp roles: 0-3 epilogue (float-float squares of the panel's columns from each raw chunk, then TMEM lanes = the
+// panel's columns), 4-7 convert (raw chunk -> s y -> tf32 hi | lo), 8 products (one thread), 9 copies (one thread,
+// TMA through the per-matrix maps).
 #include "kernels.h"
 #include "tc.cuh"
 
@@ -42,11 +43,9 @@ constexpr int ERR_TIMEOUT = 0x10;
 // mbarriers (per stage where doubled): raw chunk landed, raw chunk read (128 arrivals), operands written (128
 // arrivals), operands consumed, all products done, error drain.  Every waiter steps through a barrier's phases in
 // order from phase 0, and no barrier can run two phases ahead of a waiter.
-// per item: its products done, its accumulators read (128 arrivals), its column squares summed (128), read (128)
-enum {
-    B_RAW = 0, B_RAWFREE = 3, B_OP = 6, B_OPFREE = 8, B_DONE = 10, B_TFREE = 11, B_DSQ = 12, B_DSQFREE = 13, B_FIN = 14,
-    NBAR = 15
-};
+// a raw chunk is read by the convert warps and the epilogue warps (256 arrivals); per item: its products done, its
+// accumulators read (128 arrivals)
+enum { B_RAW = 0, B_RAWFREE = 3, B_OP = 6, B_OPFREE = 8, B_DONE = 10, B_TFREE = 11, B_FIN = 12, NBAR = 13 };
 static_assert(NBAR * 8 <= 128, "barriers below the TMEM slot");
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 static_assert(GRAM_BOX_ROWS == CH && GRAM_BOX_COLS == TILE, "one TMA box is 128 columns of one chunk");
@@ -99,8 +98,8 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
 
     if (warp == 0) tc::tmem_alloc(tmem_slot, TCOLS);
     if (tid == 0) {
-        for (int i = 0; i < NBAR; ++i)   // raw read, operands written, accumulators read, squares summed and read: 128
-            tc::mbar_init(&bars[i], ((i >= B_RAWFREE && i < B_OPFREE) || (i >= B_TFREE && i < B_FIN)) ? 128 : 1);
+        for (int i = 0; i < NBAR; ++i)   // raw read (256), operands written (128), accumulators read (128)
+            tc::mbar_init(&bars[i], (i >= B_RAWFREE && i < B_OP) ? 256 : ((i >= B_OP && i < B_OPFREE) || i == B_TFREE) ? 128 : 1);
         tc::mbar_fence_init();
         *err = 0;
     }
@@ -110,22 +109,73 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
     const uint32_t tmem = *tmem_slot;
 
     if (warp < 4) {
-        // ---------------- epilogue: row a of tile row-panel pi (TMEM lane a) ----------------
+        // ---------------- epilogue: squares of the panel's columns, then row a of tile row-panel pi (TMEM lane a) ------
+        // squares: rows 8 warp .. + 7 of each chunk, columns 4 lane .. + 3 of the panel (the first box), float-float
         const int a = warp * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+        int g = 0;   // chunk over all items
         for (int i = 0; i < nloc; ++i) {
             const Item it = item(i);
-            const uint32_t ph = (uint32_t)(i & 1);
-            const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], ph, 200) &&
-                              tc::mbar_wait_sleep(&bars[B_DSQ], ph, 200);
-            // decided per warp: tcgen05.ld needs the whole warp
-            if (!__all_sync(0xffffffffu, done && !*err)) {
+            float s = 1.0f;
+            bool scaled = false;
+            if (sc.maxbits) {
+                s = pow2_scale(__uint_as_float(sc.maxbits[it.b]));
+                scaled = true;
+            } else if (sc.s) {
+                s = sc.s[it.b];
+                scaled = true;
+            }
+            float sqh[4] = {0.f, 0.f, 0.f, 0.f}, sql[4] = {0.f, 0.f, 0.f, 0.f};
+            bool ok = true;
+            for (int c = 0; c < it.nchunks; ++c, ++g) {
+                const int rs = g % RSTAGES;
+                if (*err || !tc::mbar_wait(&bars[B_RAW + rs], par3(g))) {
+                    ok = false;
+                    break;
+                }
+                const char* raw = RAW + rs * RAW_STAGE;
+                float4 v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = *reinterpret_cast<const float4*>(raw + (8 * warp + k) * 512 + 16 * lane);
+                tc::fence_async_smem();   // generic reads before the next TMA write into the stage
+                tc::mbar_arrive(&bars[B_RAWFREE + rs]);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float4 x = v[k];
+                    if (scaled) {
+                        x.x = __fmul_rn(x.x, s); x.y = __fmul_rn(x.y, s); x.z = __fmul_rn(x.z, s); x.w = __fmul_rn(x.w, s);
+                    }
+                    ff_add_sq(sqh[0], sql[0], x.x);
+                    ff_add_sq(sqh[1], sql[1], x.y);
+                    ff_add_sq(sqh[2], sql[2], x.z);
+                    ff_add_sq(sqh[3], sql[3], x.w);
+                }
+            }
+            // the item's column sums of squares: the warps' partial sums added in fp64 in warp order 0..3 (the four
+            // warps leave together or not at all: they meet at named barriers below)
+            if (!tc::bar_and(2, 128, ok)) {
+                *err = 1;
+                break;
+            }
+            for (int w = 0; w < 4; ++w) {
+                tc::bar_sync(2, 128);
+                if (warp == w) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        double* dq = &DSQ[4 * lane + j];
+                        *dq = __dadd_rn(w == 0 ? 0.0 : *dq, ff_value(sqh[j], sql[j]));
+                    }
+                }
+            }
+            tc::bar_sync(2, 128);
+            const double d = DSQ[a];
+            const bool done = !*err && tc::mbar_wait_sleep(&bars[B_DONE], (uint32_t)(i & 1), 200);
+            // one decision for the four warps (tcgen05.ld needs whole warps; the next item's barriers need all four)
+            if (!tc::bar_and(2, 128, done && !*err)) {
                 *err = 1;
                 break;
             }
             tc::fence_after_sync();
-            const double d = DSQ[a];
-            tc::mbar_arrive(&bars[B_DSQFREE]);   // the next item's squares may go in
             float* Pb = P + (size_t)(it.b * gp.S + it.sp) * gp.tiles * TILE * TILE;
             for (int cb = 0; cb < it.W / 32; ++cb) {
                 float big[32], small[32];
@@ -163,7 +213,6 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                 s = sc.s[it.b];
                 scaled = true;
             }
-            float sqh[4] = {0.f, 0.f, 0.f, 0.f}, sql[4] = {0.f, 0.f, 0.f, 0.f};   // squares of columns 4 lane .. + 3
             for (int c = 0; c < it.nchunks; ++c, ++g) {
                 const int st = g & 1, rs = g % RSTAGES;
                 if (*err || !tc::mbar_wait(&bars[B_RAW + rs], par3(g))) {
@@ -183,19 +232,16 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                 // the raw stage is released after the one proxy fence below: the next TMA load into it writes through
                 // the async proxy, so these generic reads must be ordered before it by that fence (without one, bytes
                 // of a later chunk were seen in place of chunk c's)
+                if (scaled) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    float4& x = v[0][k];
-                    if (scaled) {
-                        x.x = __fmul_rn(x.x, s); x.y = __fmul_rn(x.y, s); x.z = __fmul_rn(x.z, s); x.w = __fmul_rn(x.w, s);
-                    }
-                    ff_add_sq(sqh[0], sql[0], x.x);
-                    ff_add_sq(sqh[1], sql[1], x.y);
-                    ff_add_sq(sqh[2], sql[2], x.z);
-                    ff_add_sq(sqh[3], sql[3], x.w);
-                    if (it.nbox == 2 && scaled) {
-                        float4& y = v[1][k];
-                        y.x = __fmul_rn(y.x, s); y.y = __fmul_rn(y.y, s); y.z = __fmul_rn(y.z, s); y.w = __fmul_rn(y.w, s);
+                    for (int h = 0; h < 2; ++h) {
+                        if (h < it.nbox) {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                float4& x = v[h][k];
+                                x.x = __fmul_rn(x.x, s); x.y = __fmul_rn(x.y, s); x.z = __fmul_rn(x.z, s); x.w = __fmul_rn(x.w, s);
+                            }
+                        }
                     }
                 }
                 if (g >= 2 && !tc::mbar_wait(&bars[B_OPFREE + st], ring_parity(g - 2))) {   // products of g - 2 done
@@ -217,25 +263,6 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
                 tc::mbar_arrive(&bars[B_RAWFREE + rs]);
                 tc::mbar_arrive(&bars[B_OP + st]);
             }
-            if (!ok) break;
-            // the item's column sums of squares, the warps' partial sums added in fp64 in warp order 0..3, once the
-            // epilogue has read the previous item's
-            if (i >= 1 && (*err || !tc::mbar_wait(&bars[B_DSQFREE], (uint32_t)((i - 1) & 1)))) {
-                ok = false;
-                break;
-            }
-            for (int w = 0; w < 4; ++w) {
-                tc::bar_sync(1, 128);
-                if (cw == w) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        double* d = &DSQ[4 * lane + j];
-                        *d = __dadd_rn(w == 0 ? 0.0 : *d, ff_value(sqh[j], sql[j]));
-                    }
-                }
-            }
-            tc::bar_sync(1, 128);
-            tc::mbar_arrive(&bars[B_DSQ]);
         }
         if (!ok) *err = 1;
     } else if (warp == 8) {

@@ -11,10 +11,10 @@
 // in separate accumulators) and is written to the partial tiles P[b][split][tile] of k_gram_tc (the same layout, so
 // k_gram_reduce sums them unchanged); the tile diagonal is replaced by the sum of squares kept in float-float (exact
 // squares, about 44 bits).
-// Persistent: one CTA per SM walks the items (panel-major, so that every CTA gets items of both panels); the chunk
-// rings run on from item to item, so the next item's copies and conversions proceed during an item's epilogue, and
-// the products resume as soon as the epilogue has read the accumulators out of TMEM.  Each item's arithmetic is the
-// same whichever CTA computes it.
+// Persistent: one CTA per SM walks the items (the two panels of a split side by side, every CTA alternating panels
+// from round to round); the chunk rings run on from item to item, so the next item's copies and conversions proceed
+// during an item's epilogue, and the products resume as soon as the epilogue has read the accumulators out of TMEM.
+// Each item's arithmetic is the same whichever CTA computes it.
 // Warp roles: 0-3 epilogue (float-float squares of the panel's columns from each raw chunk, then TMEM lanes = the
 // panel's columns), 4-7 convert (raw chunk -> s y -> tf32 hi | lo), 8 products (one thread), 9 copies (one thread,
 // TMA through the per-matrix maps).
@@ -75,7 +75,6 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
     volatile int* err = reinterpret_cast<volatile int*>(sm + OFF_BAR + 132);
 
     const int nloc = (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // this CTA's items
-    const int per_panel = gp.S * (items / (gp.S * gp.nt));                               // S x B
     // item i of this CTA: panel pi, matrix b, split sp; its width, boxes, first row and chunks
     struct Item {
         int pi, b, sp, N, nbox, W, k0, nchunks;
@@ -83,10 +82,16 @@ __global__ void __launch_bounds__(NT, 1) k_gram_ws(PtrArg p, Src src, int K, int
     auto item = [&](int i) {
         Item it;
         const int t = (int)blockIdx.x + i * (int)gridDim.x;
-        it.pi = t / per_panel;
-        const int rem = t - it.pi * per_panel;
-        it.b = rem / gp.S;
-        it.sp = rem - it.b * gp.S;
+        // items 2u and 2u + 1 are the two panels of one split (so they run side by side and share its rows in L2),
+        // their order flipped from one round of the grid to the next (so every CTA alternates panels)
+        int u = t;
+        it.pi = 0;
+        if (gp.nt == 2) {
+            u = t >> 1;
+            it.pi = (t & 1) ^ (((t & ~1) / (int)gridDim.x) & 1);
+        }
+        it.b = u / gp.S;
+        it.sp = u - it.b * gp.S;
         it.N = n - it.pi * TILE;
         it.nbox = it.N > TILE ? 2 : 1;
         it.W = it.nbox * TILE;

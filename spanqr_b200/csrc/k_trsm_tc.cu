@@ -15,9 +15,9 @@
 // Block c's row tile, its operand and later Y_c share one slot of a ring of three (raw -> hi | lo -> Y_c hi | lo), so
 // the update by Y_j never waits for a buffer the next block needs.  Product order, fixed in code:
 //   diag(0); [ACC]; then for j = 0 .. nb-2:  diag(j+1) (before Y_j exists: it overlaps block j's epilogue);
-//   T1(j) = Y_j W_{j+1,j}^T into block j+1 (32 columns); [ACC: block j+1 complete];
-//   T2(j) = Y_j W_{j+2.., j}^T into the later blocks (one product, N up to 192); [FREE of slot j % 3];
-// so the chain from one block to the next is the epilogue and T1 alone.
+//   T(j) = Y_j W_{j+1.., j}^T into every later block (one product, N = 32 (nb - 1 - j)); [ACC: block j+1 complete];
+//   [FREE of slot j % 3].
+// A product costs the same whatever its N, so one stacked update per step is cheaper than splitting off block j+1.
 // The output block j is written to Q (in place in passes 2 and 3: block j was read before, later blocks are untouched).
 // One launch solves one panel of at most 8 blocks, j0 .. j0 + nbp - 1, of a matrix of NB = n / 32 blocks (W indexed in
 // the whole image); a second panel starts its accumulators from `init`, the first panel's contribution
@@ -48,8 +48,8 @@ constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;
 constexpr uint32_t TCOLS = 512;                 // block c: large at 32 c, small at 256 + 32 c
 constexpr int ERR_TIMEOUT = 0x40;
 // mbarriers: row tile landed (per slot), diagonal W landed (x2), trailing W landed (x2), operand converted (per slot,
-// 128 arrivals), Y_j stored (128 arrivals), accumulator of the next block complete, slot released (per slot: T1 and
-// T2 of its Y and everything issued before them done), error drain.  A parity wait is only meaningful for the phase
+// 128 arrivals), Y_j stored (128 arrivals), accumulator of the next block complete, slot released (per slot: the update
+// by its Y and everything issued before it done), error drain.  A parity wait is only meaningful for the phase
 // in progress or the one just completed: every waiter below steps through its barrier's phases in order from phase 0,
 // and no barrier can run two phases ahead of a waiter, because its next phase needs something that waiter has not yet
 // released (the copy thread's one wait on ACC phase 0 comes before it issues the diagonal tile that ACC phase 2

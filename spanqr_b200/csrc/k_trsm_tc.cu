@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(NT, 1) k_trsm_tc(PtrArg p, Src src, int K, int
                 if (ok) issue_wd(2);
             }
             for (int j = 0; ok && j + 2 < nb; ++j) {
-                // slot j % 3 released: T1(j), T2(j) and diag(j + 1) (issued before them) are complete
+                // slot j % 3 released: T(j) and diag(j + 1) (issued before it) are complete
                 ok = !*err && tc::mbar_wait(&bars[B_FREE + j % NSLOT], par3(j));
                 if (!ok) break;
                 if (j + 3 < nb) {

@@ -377,14 +377,15 @@ cudaError_t launch_c(float* A, float* L, float* Li, int n, int B, const double* 
 }
 }  // namespace
 
-// CTAs per matrix: 8 above r 256 (the tiles need the shared memory of 8 SMs).  Up to r 256 each matrix spreads over
-// up to 8 SMs (at most one per block row) while the whole batch stays within half of the SMs: a lone matrix or a
-// small batch (a rank's share of a multi-GPU batch) runs at the cluster's latency, a large batch one CTA per matrix
-// (the most work per SM; its parts run on concurrent streams, so the SMs are busy anyway).  The bits do not depend on
-// the cluster size.
+// CTAs per matrix: 8 above r 256 (the tiles need the shared memory of 8 SMs).  Up to r 256 a batch of 16 or more
+// matrices runs one CTA per matrix (the most work per SM; its parts run on concurrent streams, so the SMs are busy
+// anyway: config 3's parts of 24 run 2.6% faster so than on clusters of 2), and a smaller batch (a lone matrix, a
+// rank's share of a multi-GPU batch) spreads each matrix over up to 8 SMs (at most one per block row) while the whole
+// batch stays within half of the SMs.  The bits do not depend on the cluster size.
 int chol_cluster_size(int n, int B, int nsm) {
     const int nb = n / TB;
     if (nb > 8) return 8;
+    if (B >= 16) return 1;
     int C = 1;
     while (C < 8 && 2 * C <= nb && (long long)B * 2 * C <= nsm / 2) C *= 2;
     return C;

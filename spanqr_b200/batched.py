@@ -129,7 +129,7 @@ def _run_group(Xs, Qs, stream):
 
 
 SPLIT_MIN = 16   # a shape group of at least this many matrices runs as NSTREAMS parts on as many streams
-NSTREAMS = 4
+NSTREAMS = 2      # config 3 on one B200, A/B on one box: 1 part 25.6k, 2 27.2k, 3 27.2k, 4 26.9k, 6 26.6k matrices/s
 WAVES = 4        # waves per rank under torch.distributed with gather=True (list inputs); 2 GPUs, config 3:
                  # 3.02 ms per step in one wave, 2.82 in four (2.55 without the gather)
 _SIDE = {}

@@ -345,6 +345,17 @@ def orth_latency(device, hbm):
     return rows
 
 
+def gather_desc(world):
+    """how the timed calls exchanged results between the ranks"""
+    from spanqr_b200 import batched as _batched
+    if world == 1:
+        return "none (1 GPU)"
+    if _batched.exchange_mode() == "peer":
+        return (f"peer pulls: each rank's {_batched.WAVES} waves write into its IPC-mapped slab; per wave a one-element "
+                f"NCCL all-reduce as the barrier, then one copy-engine copy per owner over NVLink")
+    return f"NCCL all_gather_into_tensor per wave, {_batched.WAVES} waves overlapped with compute"
+
+
 def main():
     a = parse()
     spec = workload_spec(a.workload, a.batch)
@@ -471,8 +482,7 @@ def main():
             "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": spec["desc"], "batch": B, "partition": "contiguous blocks by cost",
-                       "gather": f"NCCL all_gather_into_tensor per wave, {_batched.WAVES} waves overlapped with "
-                                 f"compute" if world > 1 else "none (1 GPU)",
+                       "gather": gather_desc(world),
                        "l2": "inputs larger than L2 (352 MB per step for config 3), no flush"},
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "peak_source": src, "traffic": ncu_traffic(dom),

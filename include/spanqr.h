@@ -217,6 +217,23 @@ int spanqr_read_status(const void* ws, spanqr_stream_t stream, int* device_statu
  */
 int spanqr_selftest_timeout(void* ws, size_t ws_bytes, long long limit_ns, int arrive, spanqr_stream_t stream);
 
+/*
+ * Exchange slabs of orth_batched across the GPUs of one node (no reference counterpart: the reference is single-GPU;
+ * these serve the all-gather of results when a batch is spread over 2-8 GPUs).  Every rank allocates one slab
+ * (cudaMalloc) and exports it as a SPANQR_PEER_HANDLE_BYTES-byte CUDA IPC handle; every other rank of the node opens
+ * that handle into a pointer of its own device's address space (peer access enabled on first use).  A rank's waves
+ * write their Q into its own slab and every rank then pulls each owner's run from that owner's slab with
+ * spanqr_peer_copy: one cudaMemcpyAsync, so the copy engines carry it over NVLink and no SM is taken from the waves
+ * still computing.  The caller orders the copies after the owner's writes (a stream-ordered barrier across the ranks)
+ * and closes every opened handle before the owner frees its slab.
+ */
+#define SPANQR_PEER_HANDLE_BYTES 64
+int spanqr_peer_slab_alloc(size_t bytes, void** ptr, void* handle);
+int spanqr_peer_slab_open(const void* handle, void** ptr);
+int spanqr_peer_slab_close(void* ptr);
+int spanqr_peer_slab_free(void* ptr);
+int spanqr_peer_copy(void* dst, const void* src, size_t bytes, spanqr_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,11 @@ SIGNATURES = {
     "spanqr_timing_collect": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_LL), _I]),
     "spanqr_kernel_kinds": (_I, []),
     "spanqr_kernel_kind_name": (ctypes.c_char_p, [_I]),
+    "spanqr_peer_slab_alloc": (_I, [_SZ, ctypes.POINTER(_P), _P]),
+    "spanqr_peer_slab_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "spanqr_peer_slab_close": (_I, [_P]),
+    "spanqr_peer_slab_free": (_I, [_P]),
+    "spanqr_peer_copy": (_I, [_P, _P, _SZ, _P]),
 }
 
 _lib = None

@@ -11,7 +11,11 @@ slabs are exchanged over NCCL (all_gather_into_tensor when the slabs are equal, 
 rank returns every Q.  With gather=False each rank returns only its own Qs (None elsewhere).  For a list input each
 rank computes its share in WAVES waves (consecutive runs of its matrices), the earlier waves on higher-priority streams,
 and the output is laid out wave by wave, owner by owner inside a wave: wave w's exchange, issued on one exchange stream
-in wave order, runs while wave w+1 still computes.
+in wave order, runs while wave w+1 still computes.  By default (EXCHANGE "peer") that exchange needs no SM: each rank's
+waves write into its exchange slab (PeerSlabs: one cudaMalloc per rank, mapped into every other rank through CUDA IPC),
+a one-element NCCL all-reduce per wave is the barrier that says every owner's run is written, and every rank pulls the
+runs into its output with one copy-engine copy per owner over NVLink.  EXCHANGE "nccl" (or slabs that cannot be mapped
+on some rank, decided by all ranks together) keeps the all_gather_into_tensor per wave.
 
 Host-resident matrices (CPU tensors, pinned for the copies to overlap): the batch is cut into chunks (HOST_CHUNKS), and
 per chunk the copy in (one stream), the orth (HOST_COMPUTE streams in turn) and the copy out (one stream) run on the
@@ -20,6 +24,9 @@ and the kernels.  Results land in `out` (pinned CPU
 tensors) or in newly allocated pinned tensors; under torch.distributed each rank computes and returns its own share
 (gather=False).
 """
+import ctypes
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -110,6 +117,122 @@ def exchange(out, slab, sizes, group=None):
              for q in range(world) if sizes[q] > 0]
     for w in works:
         w.wait()
+
+
+def pull_plan(b, world):
+    """the copies of one wave's exchange by peer pulls: (owner, offset, count) per owner with a non-empty run, b the
+    wave's bounds (owner q's run is b[q]..b[q + 1] of the flat buffer, in floats)"""
+    return [(q, b[q], b[q + 1] - b[q]) for q in range(world) if b[q + 1] > b[q]]
+
+
+EXCHANGE = os.environ.get("SPANQR_EXCHANGE", "peer")   # "peer" or "nccl": the same on every rank
+PULL_STREAMS = 1       # streams the pulls are spread over (owner q on stream q % PULL_STREAMS).  2 B200s, 44 MB per
+                       # copy, both ranks at once: one copy-engine copy pulls 590 GB/s, the same bytes cut in 2 / 4 / 8
+                       # copies on as many streams 550 / 450 / 380 GB/s (a local copy 1.94 TB/s alone, 0.83 on 4)
+
+
+class _SlabArray:
+    """a device pointer as a __cuda_array_interface__ object: torch.as_tensor wraps it without a copy"""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+class PeerSlabs:
+    """one exchange slab of `nbytes` on every rank of `group`, each mapped into every other rank (CUDA IPC handles
+    exchanged with all_gather_object).  Collective: every rank constructs it with the same size.  `ok` is False on
+    every rank when any rank could not allocate or map (the caller then uses the NCCL exchange)."""
+
+    def __init__(self, dev, nbytes, group):
+        L = _lib.lib()
+        self.dev, self.nbytes, self.group = dev, nbytes, group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.own, self.opened, self.ptrs, self.ok = None, [], None, False
+        with torch.cuda.device(dev):
+            ptr = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(64)
+            rc = L.spanqr_peer_slab_alloc(nbytes, ctypes.byref(ptr), handle)
+            if rc == 0:
+                self.own = ptr.value
+            handles = [None] * self.world
+            dist.all_gather_object(handles, (rc, handle.raw), group=group)
+            ok = all(h[0] == 0 for h in handles)
+            ptrs = [0] * self.world
+            for q in range(self.world):
+                if not ok:
+                    break
+                if q == self.rank:
+                    ptrs[q] = self.own
+                    continue
+                pq = ctypes.c_void_p()
+                if L.spanqr_peer_slab_open(handles[q][1], ctypes.byref(pq)) != 0:
+                    ok = False
+                    break
+                self.opened.append(pq.value)
+                ptrs[q] = pq.value
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+            self.ok = bool(flag.item())
+            if not self.ok:
+                self.release(barrier=False)
+                return
+            self.ptrs = ptrs
+            self.local = torch.as_tensor(_SlabArray(self.own, nbytes // 4), device=dev)
+            self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.pulls = tuple(torch.cuda.Stream(dev, priority=-3) for _ in range(PULL_STREAMS))
+
+    def release(self, barrier=True):
+        """unmap the peers' slabs, then (after every rank has, when `barrier`) free this rank's own: collective"""
+        L = _lib.lib()
+        with torch.cuda.device(self.dev):
+            torch.cuda.synchronize(self.dev)
+            for p in self.opened:
+                L.spanqr_peer_slab_close(p)
+            self.opened = []
+            if barrier:
+                dist.barrier(group=self.group)
+            if self.own is not None:
+                self.local = None
+                L.spanqr_peer_slab_free(self.own)
+                self.own = None
+        self.ok = False
+
+    def pull(self, out, b, after):
+        """every owner's run of one wave, from its slab into the same place of `out`, once event `after` is done"""
+        L = _lib.lib()
+        base = out.data_ptr()
+        for q, off, n in pull_plan(b, self.world):
+            ps = self.pulls[q % len(self.pulls)]
+            ps.wait_event(after)
+            _lib.check(L.spanqr_peer_copy(base + 4 * off, self.ptrs[q] + 4 * off, 4 * n, ps.cuda_stream),
+                       f"pull of rank {q}'s run")
+
+
+_PEERS = {}
+
+
+def _peer_slabs(dev, nbytes, group):
+    """the exchange slabs of (device, group), (re)made collectively when absent or too small; None when mapping
+    failed on some rank (then for the rest of the process: the NCCL exchange)"""
+    key = (str(dev), id(group) if group is not None else None)
+    have = _PEERS.get(key)
+    if have is False:
+        return None
+    if have is not None and have.nbytes >= nbytes:
+        return have
+    if have is not None:
+        have.release()
+    slabs = PeerSlabs(dev, max(nbytes, 2 * (have.nbytes if have is not None else 0)), group)
+    _PEERS[key] = slabs if slabs.ok else False
+    return slabs if slabs.ok else None
+
+
+_LAST_MODE = {}
+
+
+def exchange_mode():
+    """the exchange the last multi-GPU wave call on the current device used: "peer" or "nccl" (None before one)"""
+    return _LAST_MODE.get(str(torch.device("cuda", torch.cuda.current_device())))
 
 
 def _run_group(Xs, Qs, stream):
@@ -352,16 +475,25 @@ def orth_batched(Xs, *, gather=True, group=None, out=None, chunks=None):
 def _waves(Xs, owner, world, rank, group, nwaves):
     """the distributed gather path in waves: wave w of this rank computes on a stream of priority
     _wave_priority(w, nwaves) (parts on side streams of that priority); its exchange is issued on one exchange stream
-    that waits for that wave only, so the next waves' kernels overlap it.  All exchanges of a call go through that one
-    stream in wave order (a collective issued with async_op=False runs on the current stream, and two collectives of
-    one communicator must not run at once), and every rank issues those of the non-empty waves in the same order."""
+    that waits for that wave only, so the next waves' kernels overlap it.  All collectives of a call go through that
+    one stream in wave order (a collective issued with async_op=False runs on the current stream, and two collectives
+    of one communicator must not run at once), and every rank issues those of the non-empty waves in the same order.
+    With peer slabs the collective of a wave is a one-element all-reduce (a barrier: when it completes on a rank, every
+    rank's wave w kernels, which precede it on their streams, are done) and the pulls follow it on the pull streams;
+    one more all-reduce after the last pulls keeps the slabs from being rewritten while a peer still reads them."""
     dev = Xs[0].device
     wave = wave_of(owner, world, nwaves)
     offs, bounds = wave_layout([x.numel() for x in Xs], owner, world, wave, nwaves)
+    total = bounds[-1][world]
     with torch.cuda.device(dev):
+        peers = _peer_slabs(dev, 4 * total, group) if EXCHANGE == "peer" else None
+        _LAST_MODE[str(dev)] = "nccl" if peers is None else "peer"
         cur = torch.cuda.current_stream(dev)
-        out = torch.empty(bounds[-1][world], dtype=torch.float32, device=dev)
+        out = torch.empty(total, dtype=torch.float32, device=dev)
         Qs = [out[offs[i]:offs[i] + Xs[i].numel()].view(Xs[i].shape) for i in range(len(Xs))]
+        # this rank's waves write into its exchange slab (same offsets as `out`) when the peers pull from there
+        dst = Qs if peers is None else [peers.local[offs[i]:offs[i] + Xs[i].numel()].view(Xs[i].shape)
+                                        if owner[i] == rank else None for i in range(len(Xs))]
         for K, r in {tuple(Xs[i].shape) for i in range(len(Xs)) if owner[i] == rank}:
             zdust(K, r, dev)   # drawn on the caller's stream, which every wave's stream follows
         xs_stream = _wave_stream(dev, -1, nwaves)
@@ -375,11 +507,23 @@ def _waves(Xs, owner, world, rank, group, nwaves):
             s.wait_stream(cur)
             with torch.cuda.stream(s):
                 mine = [i for i in range(len(Xs)) if owner[i] == rank and wave[i] == w]
-                _run_local([Xs[i] for i in mine], [Qs[i] for i in mine], _wave_priority(w, nwaves))
+                _run_local([Xs[i] for i in mine], [dst[i] for i in mine], _wave_priority(w, nwaves))
             used.append(s)
             xs_stream.wait_stream(s)
             with torch.cuda.stream(xs_stream):
-                exchange(out[b[0]:b[world]], [x - b[0] for x in b], [b[q + 1] - b[q] for q in range(world)], group)
+                if peers is None:
+                    exchange(out[b[0]:b[world]], [x - b[0] for x in b], [b[q + 1] - b[q] for q in range(world)], group)
+                else:
+                    dist.all_reduce(peers.flag, group=group)   # every owner's run of wave w is in its slab
+            if peers is not None:
+                peers.pull(out, b, xs_stream.record_event())
+        if peers is not None:
+            # no rank writes its slab again (its next call's waves follow this call on its stream) while another
+            # still pulls from it
+            for ps in peers.pulls:
+                xs_stream.wait_stream(ps)
+            with torch.cuda.stream(xs_stream):
+                dist.all_reduce(peers.flag, group=group)
         for s in used:
             cur.wait_stream(s)
     return Qs

@@ -786,6 +786,55 @@ int spanqr_selftest_timeout(void* ws, size_t ws_bytes, long long limit_ns, int a
     return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
 }
 
+// ---- exchange slabs of orth_batched across the GPUs of one node (no reference counterpart) ----
+static_assert(sizeof(cudaIpcMemHandle_t) == SPANQR_PEER_HANDLE_BYTES, "IPC handle size");
+
+int spanqr_peer_slab_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle || bytes == 0) return SPANQR_ERR_ARG;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e);
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return SPANQR_OK;
+}
+
+int spanqr_peer_slab_open(const void* handle, void** ptr) {
+    if (!handle || !ptr) return SPANQR_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e);
+    *ptr = p;
+    return SPANQR_OK;
+}
+
+int spanqr_peer_slab_close(void* ptr) {
+    if (!ptr) return SPANQR_ERR_ARG;
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_peer_slab_free(void* ptr) {
+    if (!ptr) return SPANQR_ERR_ARG;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
+int spanqr_peer_copy(void* dst, const void* src, size_t bytes, spanqr_stream_t stream) {
+    if (bytes == 0) return SPANQR_OK;
+    if (!dst || !src) return SPANQR_ERR_ARG;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? SPANQR_OK : cuda_fail(e);
+}
+
 int spanqr_read_status(const void* ws, spanqr_stream_t stream, int* device_status) {
     if (!ws || !device_status) return SPANQR_ERR_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

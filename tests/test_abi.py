@@ -117,6 +117,22 @@ def test_borth_argument_checks_before_any_device_work():
     assert L.spanqr_borth_f32(al, 768, far, 768, 2048, 768, al, al + 16, need, None) == WS   # workspace misaligned
 
 
+def test_peer_slab_argument_checks_before_any_device_work():
+    """the exchange-slab entry points reject null or empty arguments without a CUDA call; an empty copy is a no-op"""
+    L = _lib.lib()
+    p = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    assert L.spanqr_peer_slab_alloc(0, ctypes.byref(p), h) == ARG
+    assert L.spanqr_peer_slab_alloc(1 << 20, None, h) == ARG
+    assert L.spanqr_peer_slab_alloc(1 << 20, ctypes.byref(p), None) == ARG
+    assert L.spanqr_peer_slab_open(None, ctypes.byref(p)) == ARG
+    assert L.spanqr_peer_slab_open(h, None) == ARG
+    assert L.spanqr_peer_slab_close(None) == ARG
+    assert L.spanqr_peer_slab_free(None) == ARG
+    assert L.spanqr_peer_copy(None, None, 0, None) == OK
+    assert L.spanqr_peer_copy(None, 1 << 20, 256, None) == ARG
+
+
 def test_error_type_names_the_code():
     with pytest.raises(_lib.SpanqrError, match="unsupported shape"):
         _lib.check(SHAPE, "orth")

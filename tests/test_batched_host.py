@@ -8,7 +8,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from spanqr_b200 import batched
-from spanqr_b200.batched import partition, layout, exchange, wave_of, wave_layout
+from spanqr_b200.batched import partition, layout, exchange, wave_of, wave_layout, pull_plan
 
 
 def test_partition_equal_costs_is_contiguous_and_balanced():
@@ -47,6 +47,25 @@ def test_partition_mixed_batch_balances_cost_exactly():
     loads = [sum(c for c, q in zip(costs, o) if q == w) for w in range(8)]
     assert len(set(loads)) == 1
     assert partition(costs, 8) == o                          # deterministic
+
+
+@pytest.mark.parametrize("numels", [[4, 4, 4, 4, 4, 4, 4, 4], [9, 1, 7, 3, 5, 2], [6, 6, 1]])
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_pull_plan_tiles_every_wave(numels, world):
+    """the peer pulls of all waves together copy every float of the output exactly once, each owner's run from the
+    owner that computed it"""
+    owner = partition(numels, world)
+    wave = wave_of(owner, world, 4)
+    offs, bounds = wave_layout(numels, owner, world, wave, 4)
+    seen = [None] * bounds[-1][world]
+    for b in bounds:
+        for q, off, n in pull_plan(b, world):
+            assert n > 0
+            for k in range(off, off + n):
+                assert seen[k] is None
+                seen[k] = q
+    for i, n in enumerate(numels):
+        assert seen[offs[i]:offs[i] + n] == [owner[i]] * n
 
 
 def test_layout_owner_major():

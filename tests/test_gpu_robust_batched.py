@@ -133,10 +133,19 @@ def _rank_main(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
-        Xs = [cases.cfg4_matrix(i, n_small=6, K_small=1024, K_big=2048, N=512).cuda() for i in range(9)]
-        Qs = orth_batched(Xs)
+        from spanqr_b200 import batched
+        Xs = [cases.cfg4_matrix(i, n_small=6, K_small=1024, K_big=2048, N=512).cuda() for i in range(12)]
+        runs = []
+        # peer pulls: first call maps the slabs, the second (larger) regrows them, the third reuses them
+        for n in (9, 12, 9):
+            Qs = orth_batched(Xs[:n])
+            torch.cuda.synchronize()
+            runs.append(("peer", batched.exchange_mode(), [x.cpu() for x in Qs]))
+        batched.EXCHANGE = "nccl"
+        Qs = orth_batched(Xs[:9])
         torch.cuda.synchronize()
-        q.put((rank, [x.cpu() for x in Qs]))
+        runs.append(("nccl", batched.exchange_mode(), [x.cpu() for x in Qs]))
+        q.put((rank, runs))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -144,8 +153,10 @@ def _rank_main(rank, world, port, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_multi_gpu_matches_single_gpu_bitwise():
+    """2 ranks, every result with the single-GPU bits: through the peer-pull exchange (slabs mapped, regrown for a
+    larger batch, reused) and through the NCCL all-gather"""
     import torch.multiprocessing as mp
-    Xs = [cases.cfg4_matrix(i, n_small=6, K_small=1024, K_big=2048, N=512).cuda() for i in range(9)]
+    Xs = [cases.cfg4_matrix(i, n_small=6, K_small=1024, K_big=2048, N=512).cuda() for i in range(12)]
     want = [orth(x).cpu() for x in Xs]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -157,7 +168,10 @@ def test_multi_gpu_matches_single_gpu_bitwise():
     for p in procs:
         p.join(timeout=120)
     for rank in range(2):
-        assert all(_bits(a, b) for a, b in zip(res[rank], want)), rank
+        for mode, used, Qs in res[rank]:
+            assert used == mode, (rank, mode, used)
+            assert len(Qs) in (9, 12)
+            assert all(_bits(a, b) for a, b in zip(Qs, want)), (rank, mode, len(Qs))
 
 
 def test_concurrent_streams_bitwise_stress():

@@ -174,7 +174,7 @@ class PeerSlabs:
             dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
             self.ok = bool(flag.item())
             if not self.ok:
-                self.release(barrier=False)
+                self.release()   # every rank reaches this (the MIN above), and unmaps before any owner frees
                 return
             self.ptrs = ptrs
             self.local = torch.as_tensor(_SlabArray(self.own, nbytes // 4), device=dev)

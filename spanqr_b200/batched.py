@@ -212,10 +212,13 @@ _PEERS = {}
 
 
 def _peer_slabs(dev, nbytes, group):
-    """the exchange slabs of (device, group), (re)made collectively when absent or too small; None when mapping
-    failed on some rank (then for the rest of the process: the NCCL exchange)"""
-    key = (str(dev), id(group) if group is not None else None)
-    have = _PEERS.get(key)
+    """the exchange slabs of (device, process group), (re)made collectively when absent or too small; None when
+    mapping failed on some rank (then, for that group, the NCCL exchange).  The key holds the group object itself
+    (WORLD's for None), so a process group created after another was destroyed never finds the old group's slabs."""
+    g = group if group is not None else dist.group.WORLD
+    key = (str(dev), id(g))
+    entry = _PEERS.get(key)
+    have = entry[1] if entry is not None and entry[0] is g else None
     if have is False:
         return None
     if have is not None and have.nbytes >= nbytes:
@@ -223,7 +226,7 @@ def _peer_slabs(dev, nbytes, group):
     if have is not None:
         have.release()
     slabs = PeerSlabs(dev, max(nbytes, 2 * (have.nbytes if have is not None else 0)), group)
-    _PEERS[key] = slabs if slabs.ok else False
+    _PEERS[key] = (g, slabs if slabs.ok else False)
     return slabs if slabs.ok else None
 
 

@@ -68,6 +68,40 @@ def test_pull_plan_tiles_every_wave(numels, world):
         assert seen[offs[i]:offs[i] + n] == [owner[i]] * n
 
 
+def test_peer_slab_cache(monkeypatch):
+    """exchange slabs are made once per (device, group), reused while large enough, regrown (old ones released first)
+    to at least twice their size, never retried for a group whose mapping failed, and kept apart per group object"""
+    from spanqr_b200 import batched
+    made = []
+
+    class FakeSlabs:
+        def __init__(self, dev, nbytes, group):
+            self.nbytes, self.group, self.released = nbytes, group, False
+            self.ok = not getattr(group, "fail", False)
+            made.append(self)
+
+        def release(self):
+            self.released = True
+
+    class Group:
+        def __init__(self, fail=False):
+            self.fail = fail
+
+    monkeypatch.setattr(batched, "PeerSlabs", FakeSlabs)
+    monkeypatch.setattr(batched, "_PEERS", {})
+    g1, g2, bad = Group(), Group(), Group(fail=True)
+    a = batched._peer_slabs("cuda:0", 1000, g1)
+    assert a is made[0] and a.nbytes == 1000
+    assert batched._peer_slabs("cuda:0", 800, g1) is a
+    b = batched._peer_slabs("cuda:0", 1500, g1)
+    assert a.released and b is made[1] and b.nbytes == 2000
+    c = batched._peer_slabs("cuda:0", 100, g2)
+    assert c is made[2] and c is not b
+    assert batched._peer_slabs("cuda:1", 100, g1) is made[3]
+    assert batched._peer_slabs("cuda:0", 100, bad) is None
+    assert batched._peer_slabs("cuda:0", 100, bad) is None and len(made) == 5
+
+
 def test_layout_owner_major():
     owner = [1, 0, 1, 0, 2]
     offs, slab, sizes = layout([4, 5, 6, 7, 8], owner, 3)

@@ -126,6 +126,7 @@ def pull_plan(b, world):
 
 
 EXCHANGE = os.environ.get("SPANQR_EXCHANGE", "peer")   # "peer" or "nccl": the same on every rank
+PEER_HANDLE_BYTES = 64  # SPANQR_PEER_HANDLE_BYTES
 PULL_STREAMS = 1       # streams the pulls are spread over (owner q on stream q % PULL_STREAMS).  2 B200s, 44 MB per
                        # copy, both ranks at once: one copy-engine copy pulls 590 GB/s, the same bytes cut in 2 / 4 / 8
                        # copies on as many streams 550 / 450 / 380 GB/s (a local copy 1.94 TB/s alone, 0.83 on 4)
@@ -150,7 +151,7 @@ class PeerSlabs:
         self.own, self.opened, self.ptrs, self.ok = None, [], None, False
         with torch.cuda.device(dev):
             ptr = ctypes.c_void_p()
-            handle = ctypes.create_string_buffer(64)
+            handle = ctypes.create_string_buffer(PEER_HANDLE_BYTES)
             rc = L.spanqr_peer_slab_alloc(nbytes, ctypes.byref(ptr), handle)
             if rc == 0:
                 self.own = ptr.value
@@ -181,16 +182,15 @@ class PeerSlabs:
             self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
             self.pulls = tuple(torch.cuda.Stream(dev, priority=-3) for _ in range(PULL_STREAMS))
 
-    def release(self, barrier=True):
-        """unmap the peers' slabs, then (after every rank has, when `barrier`) free this rank's own: collective"""
+    def release(self):
+        """unmap the peers' slabs, then, once every rank has, free this rank's own: collective"""
         L = _lib.lib()
         with torch.cuda.device(self.dev):
             torch.cuda.synchronize(self.dev)
             for p in self.opened:
                 L.spanqr_peer_slab_close(p)
             self.opened = []
-            if barrier:
-                dist.barrier(group=self.group)
+            dist.barrier(group=self.group)
             if self.own is not None:
                 self.local = None
                 L.spanqr_peer_slab_free(self.own)

@@ -489,6 +489,8 @@ def _waves(Xs, owner, world, rank, group, nwaves):
     offs, bounds = wave_layout([x.numel() for x in Xs], owner, world, wave, nwaves)
     total = bounds[-1][world]
     with torch.cuda.device(dev):
+        if EXCHANGE not in ("peer", "nccl"):
+            raise ValueError(f"SPANQR_EXCHANGE / batched.EXCHANGE must be 'peer' or 'nccl', not {EXCHANGE!r}")
         peers = _peer_slabs(dev, 4 * total, group) if EXCHANGE == "peer" else None
         _LAST_MODE[str(dev)] = "nccl" if peers is None else "peer"
         cur = torch.cuda.current_stream(dev)

@@ -219,9 +219,10 @@ int spanqr_selftest_timeout(void* ws, size_t ws_bytes, long long limit_ns, int a
 
 /*
  * Exchange slabs of orth_batched across the GPUs of one node (no reference counterpart: the reference is single-GPU;
- * these serve the all-gather of results when a batch is spread over 2-8 GPUs).  Every rank allocates one slab
- * (cudaMalloc) and exports it as a SPANQR_PEER_HANDLE_BYTES-byte CUDA IPC handle; every other rank of the node opens
- * that handle into a pointer of its own device's address space (peer access enabled on first use).  A rank's waves
+ * these serve the all-gather of results when a batch is spread over 2-8 GPUs).  Every rank allocates one slab on its
+ * current device (cudaMalloc) and exports it as a SPANQR_PEER_HANDLE_BYTES-byte CUDA IPC handle; every other rank of
+ * the node, with its own device current, opens that handle into a pointer it can read (peer access enabled on first
+ * use).  A handle cannot be opened by the process that exported it.  A rank's waves
  * write their Q into its own slab and every rank then pulls each owner's run from that owner's slab with
  * spanqr_peer_copy: one cudaMemcpyAsync, so the copy engines carry it over NVLink and no SM is taken from the waves
  * still computing.  The caller orders the copies after the owner's writes (a stream-ordered barrier across the ranks)

@@ -160,6 +160,75 @@ def _worker(rank, world, port, sizes_per_rank, q):
         dist.destroy_process_group()
 
 
+def _slab_worker(rank, world, port, what, bad_rank, q):
+    """PeerSlabs set-up on gloo ranks with a fake library whose alloc or open fails on `bad_rank`"""
+    import contextlib
+    import ctypes
+    from spanqr_b200 import batched
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    calls = []
+
+    class FakeLib:
+        def spanqr_peer_slab_alloc(self, nbytes, ptr, handle):
+            if what == "alloc" and rank == bad_rank:
+                return 4
+            ptr._obj.value = 0x10000 * (rank + 1)
+            ctypes.memmove(handle, bytes([rank + 1]) * 8, 8)
+            return 0
+
+        def spanqr_peer_slab_open(self, handle, ptr):
+            calls.append(("open", handle[0]))
+            if what == "open" and rank == bad_rank:
+                return 4
+            ptr._obj.value = 0x100 * handle[0]
+            return 0
+
+        def spanqr_peer_slab_close(self, p):
+            calls.append(("close", p))
+            return 0
+
+        def spanqr_peer_slab_free(self, p):
+            calls.append(("free", p))
+            return 0
+
+    try:
+        batched._lib.lib = lambda: FakeLib()
+        torch.cuda.device = lambda d: contextlib.nullcontext()
+        torch.cuda.synchronize = lambda *a: None
+        slabs = batched.PeerSlabs(torch.device("cpu"), 1 << 20, None)
+        q.put((rank, slabs.ok, calls))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("what,bad_rank", [("open", 1), ("open", 0), ("alloc", 1)])
+def test_peer_slabs_fail_together_on_gloo_ranks(what, bad_rank):
+    """when one rank cannot allocate or map, every rank gives up the peer exchange: each unmaps what it mapped and
+    frees its own slab (after the barrier), and none keeps a mapping"""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_slab_worker, args=(r, 2, port, what, bad_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (ok, calls) for r, ok, calls in (q.get(timeout=120) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+    for r, (ok, calls) in res.items():
+        assert ok is False, r
+        opened = [c for c in calls if c[0] == "open"]
+        closes = [c for c in calls if c[0] == "close"]
+        frees = [c for c in calls if c[0] == "free"]
+        if what == "alloc":
+            assert opened == [] and closes == []                            # nothing mapped once a handle is bad
+        else:
+            assert opened == [("open", 2 - r)]                              # the other rank's handle
+            assert len(closes) == (0 if r == bad_rank else 1)               # what was mapped is unmapped
+        assert frees == ([] if what == "alloc" and r == bad_rank else [("free", 0x10000 * (r + 1))])
+        assert calls.index(frees[0]) > max((calls.index(c) for c in closes), default=-1) if frees else True
+
+
 @pytest.mark.parametrize("sizes", [[6, 6], [5, 9]])
 def test_exchange_two_gloo_ranks(sizes):
     """equal slabs take the all-gather path, unequal ones the per-owner broadcasts"""

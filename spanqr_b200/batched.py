@@ -119,10 +119,14 @@ def exchange(out, slab, sizes, group=None):
         w.wait()
 
 
-def pull_plan(b, world):
+def pull_plan(b, world, rank=None):
     """the copies of one wave's exchange by peer pulls: (owner, offset, count) per owner with a non-empty run, b the
-    wave's bounds (owner q's run is b[q]..b[q + 1] of the flat buffer, in floats)"""
-    return [(q, b[q], b[q + 1] - b[q]) for q in range(world) if b[q + 1] > b[q]]
+    wave's bounds (owner q's run is b[q]..b[q + 1] of the flat buffer, in floats).  For `rank` the owners come in the
+    order rank + 1, rank + 2, ... (mod world), its own run last: at every position of the sequence the ranks read
+    from as many different owners, so no GPU's links serve several readers at once."""
+    first = 0 if rank is None else rank + 1
+    order = [(first + k) % world for k in range(world)]
+    return [(q, b[q], b[q + 1] - b[q]) for q in order if b[q + 1] > b[q]]
 
 
 EXCHANGE = os.environ.get("SPANQR_EXCHANGE", "peer")   # "peer" or "nccl": the same on every rank
@@ -201,7 +205,7 @@ class PeerSlabs:
         """every owner's run of one wave, from its slab into the same place of `out`, once event `after` is done"""
         L = _lib.lib()
         base = out.data_ptr()
-        for q, off, n in pull_plan(b, self.world):
+        for q, off, n in pull_plan(b, self.world, self.rank):
             ps = self.pulls[q % len(self.pulls)]
             ps.wait_event(after)
             _lib.check(L.spanqr_peer_copy(base + 4 * off, self.ptrs[q] + 4 * off, 4 * n, ps.cuda_stream),

@@ -68,6 +68,22 @@ def test_pull_plan_tiles_every_wave(numels, world):
         assert seen[offs[i]:offs[i] + n] == [owner[i]] * n
 
 
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_pull_plan_staggers_the_owners(world):
+    """with every run non-empty, the k-th pull of each rank reads a different owner (a permutation at every k), each
+    rank's own run comes last, and each rank's plan covers the same runs as the unordered plan"""
+    b = [10 * q for q in range(world + 1)]
+    plans = [pull_plan(b, world, r) for r in range(world)]
+    for k in range(world):
+        assert sorted(p[k][0] for p in plans) == list(range(world))
+    for r, p in enumerate(plans):
+        assert p[-1][0] == r
+        assert sorted(p) == pull_plan(b, world)
+    b = [0, 5, 5, 9]                                  # an empty run is skipped, the order kept
+    assert [q for q, _, _ in pull_plan(b, 3, 0)] == [2, 0]
+    assert [q for q, _, _ in pull_plan(b, 3, 1)] == [2, 0]
+
+
 def test_peer_slab_cache(monkeypatch):
     """exchange slabs are made once per (device, group), reused while large enough, regrown (old ones released first)
     to at least twice their size, never retried for a group whose mapping failed, and kept apart per group object"""

@@ -369,7 +369,11 @@ def main():
     device = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        # NCCL's kernels (the exchange's barriers or all-gathers) on high-priority streams: the waves run on raised
+        # priorities, and at the default priority a collective's CTAs would queue behind every wave's pending CTAs
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device, pg_options=opts)
     from spanqr_b200 import orth_batched
     from spanqr_b200 import _lib
     from spanqr_b200.batched import partition

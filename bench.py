@@ -373,6 +373,7 @@ def main():
         # priorities, and at the default priority a collective's CTAs would queue behind every wave's pending CTAs
         opts = dist.ProcessGroupNCCL.Options()
         opts.is_high_priority_stream = True
+        opts._timeout = timedelta(seconds=300)   # the same as the timeout below (torch warns when they differ)
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device, pg_options=opts)
     from spanqr_b200 import orth_batched
     from spanqr_b200 import _lib
